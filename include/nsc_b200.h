@@ -1,0 +1,201 @@
+/*
+ * nsc_b200.h -- C ABI of the B200 (sm_100a) shift-window kernel library
+ * `libnsc_b200.so`.
+ *
+ * This ABI replaces the pybind11 module `neural_shift_cuda._C` of the
+ * reference project (csrc/shift_ops.cpp:347-368, csrc/metropolis.cpp:42-48).
+ * Differences from that module, all deliberate:
+ *   - plain device pointers and int64 extents, no torch types;
+ *   - outputs and scratch are allocated by the caller; the library never
+ *     allocates device memory and never synchronizes;
+ *   - the shift table is a HOST pointer to S rows of `shift_cols` int64
+ *     values (dx, dy[, has_inv]); it is copied into the kernel parameters;
+ *   - inputs keep their storage dtype (fp16/bf16/fp32 are read natively and
+ *     promoted in registers; fp64 stays fp64) instead of being copied to a
+ *     promoted tensor first;
+ *   - a weight stack may be channel-broadcast (`w_channels == 1` while
+ *     C > 1): it is read once per pixel and applied to every channel.
+ *
+ * Layouts: images (B, C, H, W); weight stacks (S*B, w_channels, H, W) for
+ * accumulate / normalized; (B, S, w_channels, H, W) for metropolis; all
+ * contiguous row-major.  `stream` is a cudaStream_t (NULL = legacy default).
+ * Every call is asynchronous on `stream` and uses the current device.
+ * Errors: a non-zero nsc_status; nsc_last_error_string() gives the message
+ * for the calling host thread.
+ */
+#ifndef NSC_B200_H
+#define NSC_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NSC_API __attribute__((visibility("default")))
+#else
+#define NSC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nsc_status {
+    NSC_OK = 0,
+    NSC_ERR_INVALID_ARG = 1,       /* shape / pointer / shift-table error */
+    NSC_ERR_UNSUPPORTED_DTYPE = 2, /* dtype or dtype combination */
+    NSC_ERR_S_OUT_OF_RANGE = 3,    /* S outside [1, 1024] */
+    NSC_ERR_LAUNCH_FAILED = 4,     /* cudaGetLastError after a launch */
+    NSC_ERR_TIMEOUT = 5            /* a bounded device-side wait gave up */
+} nsc_status;
+
+typedef enum nsc_dtype {
+    NSC_F16 = 0,
+    NSC_BF16 = 1,
+    NSC_F32 = 2,
+    NSC_F64 = 3
+} nsc_dtype;
+
+/* ABI marker; replaces `_C.index_width_bits()` (csrc/shift_ops.cpp:351).
+ * Always 64: shifts and flattened offsets are int64 end to end. */
+NSC_API int nsc_index_width_bits(void);
+
+/* Library version string ("0.12.0-b200.N"). */
+NSC_API const char* nsc_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+NSC_API const char* nsc_last_error_string(void);
+
+/* ---------------------------------------------------------------------
+ * Gathers.  Replace shift_gather_forward / pair_gather_forward
+ * (csrc/shift_ops.cpp:81-140) and their backward (shift_ops.cpp:102-156).
+ * out : (S*B, C, H, W) for shift_gather, (S*B, 2C, H, W) for pair_gather,
+ *       same dtype as guide (bit-exact copies);
+ * mask: (S*B, 1, H, W) in guide dtype, 1 where (h+dx, w+dy) is inside.
+ * Backward: grad_out in the forward output layout -> grad_guide (B,C,H,W),
+ * same dtype, accumulated in fp32 (fp64 for fp64), deterministic.
+ * shift_cols is 2 or 3 (only dx, dy are read).
+ * ------------------------------------------------------------------- */
+NSC_API nsc_status nsc_shift_gather_fwd(const void* guide, int dtype,
+                                int64_t B, int64_t C, int64_t H, int64_t W,
+                                const int64_t* shifts, int64_t S,
+                                int64_t shift_cols, void* out, void* mask,
+                                void* stream);
+NSC_API nsc_status nsc_pair_gather_fwd(const void* guide, int dtype,
+                               int64_t B, int64_t C, int64_t H, int64_t W,
+                               const int64_t* shifts, int64_t S,
+                               int64_t shift_cols, void* out, void* mask,
+                               void* stream);
+NSC_API nsc_status nsc_shift_gather_bwd(const void* grad_out, int dtype,
+                                int64_t B, int64_t C, int64_t H, int64_t W,
+                                const int64_t* shifts, int64_t S,
+                                int64_t shift_cols, void* grad_guide,
+                                void* stream);
+NSC_API nsc_status nsc_pair_gather_bwd(const void* grad_out, int dtype,
+                               int64_t B, int64_t C, int64_t H, int64_t W,
+                               const int64_t* shifts, int64_t S,
+                               int64_t shift_cols, void* grad_guide,
+                               void* stream);
+
+/* ---------------------------------------------------------------------
+ * accumulate_uz.  Replaces accumulate_uz_forward / _backward
+ * (csrc/shift_ops.cpp:160-212).  shifts: (S, 3).
+ * x dtype / w dtype: equal, or x fp32 with w fp16/bf16; fp64 only with
+ * fp64.  U, Z, grad_x: fp32 (fp64 for fp64 inputs); grad_U, grad_Z in
+ * that same accumulator dtype.  grad_w: w's dtype and shape
+ * (S*B, w_channels, H, W); a broadcast weight receives the channel sum.
+ * ------------------------------------------------------------------- */
+NSC_API nsc_status nsc_accumulate_uz_fwd(const void* x, int x_dtype,
+                                 const void* w, int w_dtype,
+                                 int64_t w_channels,
+                                 int64_t B, int64_t C, int64_t H, int64_t W,
+                                 const int64_t* shifts, int64_t S,
+                                 void* U, void* Z, void* stream);
+NSC_API nsc_status nsc_accumulate_uz_bwd(const void* x, int x_dtype,
+                                 const void* w, int w_dtype,
+                                 int64_t w_channels,
+                                 int64_t B, int64_t C, int64_t H, int64_t W,
+                                 const int64_t* shifts, int64_t S,
+                                 const void* grad_U, const void* grad_Z,
+                                 void* grad_x, void* grad_w, void* stream);
+
+/* Row-band form of nsc_accumulate_uz_fwd for an image split into bands
+ * of rows across devices.  The caller owns output rows [row0, row0+Hb) of
+ * an image with Hg rows.  x_ext holds Hb + 2R rows: global rows
+ * row0-R .. row0+Hb+R-1, already wrapped circularly; w holds the band's
+ * Hb rows of every weight plane.  Mirror terms whose source pixel lies
+ * outside the band are NOT added here (the owner of that row adds them,
+ * see nsc_accumulate_uz_band_edges).  U, Z: (B, C, Hb, W). */
+NSC_API nsc_status nsc_accumulate_uz_band_fwd(const void* x_ext, int x_dtype,
+                                      const void* w, int w_dtype,
+                                      int64_t w_channels, int64_t B,
+                                      int64_t C, int64_t Hb, int64_t W,
+                                      int64_t row0, int64_t Hg,
+                                      const int64_t* shifts, int64_t S,
+                                      void* U, void* Z, void* stream);
+
+/* Mirror contributions of this band's own weights to the R rows just
+ * above (edge_top: global rows row0-R .. row0-1) and just below
+ * (edge_bot: rows row0+Hb .. row0+Hb+R-1) the band.  edge_top / edge_bot
+ * are (2, B, C, R, W) accumulators (U part then Z part, fp32/fp64),
+ * overwritten.  Rows outside the image [0, Hg) receive zeros. */
+NSC_API nsc_status nsc_accumulate_uz_band_edges(const void* x_ext, int x_dtype,
+                                        const void* w, int w_dtype,
+                                        int64_t w_channels, int64_t B,
+                                        int64_t C, int64_t Hb, int64_t W,
+                                        int64_t row0, int64_t Hg,
+                                        const int64_t* shifts, int64_t S,
+                                        void* edge_top, void* edge_bot,
+                                        void* stream);
+
+/* ---------------------------------------------------------------------
+ * normalized_accumulate_uz.  Replaces normalized_accumulate_uz_forward /
+ * _backward (csrc/shift_ops.cpp:218-283).  One pass per output with an
+ * online running max.  log_weights != 0: weights are logits, -inf masks.
+ * D, log_C: fp32 (fp64), shape (B, C, H, W).  Empty rows give D = 0,
+ * log_C = -inf; NaN / +inf / negative-positive-weight rows give NaN.
+ * invalid_flag (nullable, device int): the forward ORs 1 into it when a
+ * weight breaks the contract (NaN or +inf; negative in positive mode),
+ * which replaces the reference's separate validation pass (ops.py:209-224).
+ * ------------------------------------------------------------------- */
+NSC_API nsc_status nsc_normalized_accumulate_uz_fwd(
+    const void* x, int x_dtype, const void* w, int w_dtype,
+    int64_t w_channels, int64_t B, int64_t C, int64_t H, int64_t W,
+    const int64_t* shifts, int64_t S, int log_weights,
+    void* D, void* log_C, int* invalid_flag, void* stream);
+NSC_API nsc_status nsc_normalized_accumulate_uz_bwd(
+    const void* x, int x_dtype, const void* w, int w_dtype,
+    int64_t w_channels, int64_t B, int64_t C, int64_t H, int64_t W,
+    const int64_t* shifts, int64_t S, int log_weights,
+    const void* D, const void* log_C, const void* grad_D,
+    const void* grad_log_C, void* grad_x, void* grad_w, void* stream);
+
+/* ---------------------------------------------------------------------
+ * metropolis_aggregate.  Replaces `_C.metropolis_aggregate`
+ * (csrc/metropolis.cpp:29-37, metropolis_cuda.cu:195-240) and adds the
+ * backward the reference lacks.  w_half: (B, S, w_channels, H, W);
+ * img: (B, C, H, W) same dtype class as w_half.  Wx, d_hat: img dtype.
+ * degree: caller scratch (B, w_channels, H, W) in the accumulator dtype
+ * (fp32, fp64 for fp64); the forward writes the raw degree d = K e there
+ * and the backward reads it back.  grad_degree: caller scratch of the same
+ * size for the backward.  grad_w: w_half's dtype and shape; grad_img:
+ * img's dtype.
+ * ------------------------------------------------------------------- */
+NSC_API nsc_status nsc_metropolis_fwd(const void* w_half, int w_dtype,
+                              int64_t w_channels, const void* img,
+                              int x_dtype, int64_t B, int64_t C, int64_t H,
+                              int64_t W, const int64_t* shifts, int64_t S,
+                              int use_box, double eps, void* Wx, void* d_hat,
+                              void* degree, void* stream);
+NSC_API nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype,
+                              int64_t w_channels, const void* img,
+                              int x_dtype, int64_t B, int64_t C, int64_t H,
+                              int64_t W, const int64_t* shifts, int64_t S,
+                              int use_box, double eps, const void* degree,
+                              const void* d_hat, const void* grad_Wx,
+                              const void* grad_d_hat, void* grad_degree,
+                              void* grad_w, void* grad_img, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSC_B200_H */

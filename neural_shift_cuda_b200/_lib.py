@@ -1,0 +1,191 @@
+"""ctypes binding of `libnsc_b200.so` (the C ABI in include/nsc_b200.h).
+
+The library is loaded once, from this package's `_lib/` directory (built by
+`python -m neural_shift_cuda_b200.build`).  If it is missing or stale the
+ops raise at their first CUDA call with the underlying loader error, like
+the reference's `_require_cuda_ext` (`neural_shift_cuda/ops.py:510-546`).
+There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+import weakref
+from typing import Optional
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libnsc_b200.so")
+
+NSC_F16, NSC_BF16, NSC_F32, NSC_F64 = 0, 1, 2, 3
+_DTYPES = {torch.float16: NSC_F16, torch.bfloat16: NSC_BF16,
+           torch.float32: NSC_F32, torch.float64: NSC_F64}
+
+_STATUS = {0: "NSC_OK", 1: "NSC_ERR_INVALID_ARG",
+           2: "NSC_ERR_UNSUPPORTED_DTYPE", 3: "NSC_ERR_S_OUT_OF_RANGE",
+           4: "NSC_ERR_LAUNCH_FAILED", 5: "NSC_ERR_TIMEOUT"}
+
+_lib: Optional[ctypes.CDLL] = None
+_load_error: Optional[BaseException] = None
+_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_D = ctypes.c_double
+_LP = ctypes.POINTER(ctypes.c_int64)
+
+# argument lists, in header order
+_SIGS = {
+    "nsc_shift_gather_fwd": [_P, _I, _L, _L, _L, _L, _LP, _L, _L, _P, _P, _P],
+    "nsc_pair_gather_fwd": [_P, _I, _L, _L, _L, _L, _LP, _L, _L, _P, _P, _P],
+    "nsc_shift_gather_bwd": [_P, _I, _L, _L, _L, _L, _LP, _L, _L, _P, _P],
+    "nsc_pair_gather_bwd": [_P, _I, _L, _L, _L, _L, _LP, _L, _L, _P, _P],
+    "nsc_accumulate_uz_fwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _LP, _L,
+                              _P, _P, _P],
+    "nsc_accumulate_uz_bwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _LP, _L,
+                              _P, _P, _P, _P, _P],
+    "nsc_accumulate_uz_band_fwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _L,
+                                   _L, _LP, _L, _P, _P, _P],
+    "nsc_accumulate_uz_band_edges": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _L,
+                                     _L, _LP, _L, _P, _P, _P],
+    "nsc_normalized_accumulate_uz_fwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L,
+                                         _LP, _L, _I, _P, _P, _P, _P],
+    "nsc_normalized_accumulate_uz_bwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L,
+                                         _LP, _L, _I, _P, _P, _P, _P, _P, _P,
+                                         _P],
+    "nsc_metropolis_fwd": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP, _L, _I,
+                           _D, _P, _P, _P, _P],
+    "nsc_metropolis_bwd": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP, _L, _I,
+                           _D, _P, _P, _P, _P, _P, _P, _P, _P],
+}
+
+EXPORTED = ["nsc_index_width_bits", "nsc_version", "nsc_last_error_string",
+            *_SIGS]
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once); raise RuntimeError with the cause if absent."""
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        try:
+            lib = ctypes.CDLL(LIB_PATH)
+            lib.nsc_index_width_bits.restype = ctypes.c_int
+            lib.nsc_version.restype = ctypes.c_char_p
+            lib.nsc_last_error_string.restype = ctypes.c_char_p
+            for name, args in _SIGS.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = ctypes.c_int
+        except (OSError, AttributeError) as e:
+            _load_error = e
+            raise RuntimeError(
+                f"neural_shift_cuda_b200: cannot load the kernel library "
+                f"{LIB_PATH}: {type(e).__name__}: {e}. Build it with "
+                f"`python -m neural_shift_cuda_b200.build`.") from e
+        _lib = lib
+        return lib
+
+
+def available() -> bool:
+    try:
+        load()
+        return True
+    except RuntimeError:
+        return False
+
+
+def index_width_bits() -> int:
+    return int(load().nsc_index_width_bits())
+
+
+def version() -> str:
+    return load().nsc_version().decode()
+
+
+def call(name: str, *args) -> None:
+    """Call a library entry point and map a non-zero status to an error.
+
+    Argument errors raise RuntimeError with the library's message, which
+    mirrors the reference's TORCH_CHECK messages (csrc/shift_ops.cpp)."""
+    lib = load()
+    st = getattr(lib, name)(*args)
+    if st != 0:
+        msg = lib.nsc_last_error_string().decode()
+        raise RuntimeError(f"{msg} [{_STATUS.get(st, st)}]")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPES[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+# ---------------------------------------------------------------------------
+# host copies of shift tables
+# ---------------------------------------------------------------------------
+
+class HostShifts:
+    """A contiguous int64 host copy of a shift table, kept alive while the
+    ctypes pointer is in use."""
+
+    __slots__ = ("t", "S", "cols")
+
+    def __init__(self, t: torch.Tensor):
+        self.t = t
+        self.S = int(t.shape[0])
+        self.cols = int(t.shape[1])
+
+    @property
+    def ptr(self):
+        return ctypes.cast(self.t.data_ptr(), _LP)
+
+    def rows(self):
+        return [tuple(int(v) for v in r) for r in self.t.tolist()]
+
+
+_shift_cache: dict = {}
+
+
+def _drop(key):
+    _shift_cache.pop(key, None)
+
+
+def host_shifts(shifts) -> HostShifts:
+    """Int64 host copy of `shifts` ((S, 2|3) tensor, or a list of rows).
+
+    A device tensor is copied to the host once and cached per tensor object
+    and version, so a model that keeps its shift tensor on the GPU (as the
+    reference's installers do) pays one device-to-host copy, not one per
+    call."""
+    if not isinstance(shifts, torch.Tensor):
+        rows = [[int(v) for v in r] for r in shifts]
+        t = torch.tensor(rows, dtype=torch.int64).reshape(len(rows), -1)
+        return HostShifts(t.contiguous())
+    if shifts.device.type == "cpu":
+        return HostShifts(shifts.detach().to(torch.int64).contiguous())
+    key = id(shifts)
+    hit = _shift_cache.get(key)
+    ver = shifts._version
+    if hit is not None and hit[0]() is shifts and hit[1] == ver:
+        return hit[2]
+    hs = HostShifts(shifts.detach().to("cpu", torch.int64).contiguous())
+    _shift_cache[key] = (weakref.ref(shifts), ver, hs)
+    weakref.finalize(shifts, _drop, key)
+    return hs

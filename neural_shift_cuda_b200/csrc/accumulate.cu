@@ -1,0 +1,462 @@
+// accumulate.cu -- accumulate_uz forward / backward (generic path) and the
+// row-band forward used when one image is split over several GPUs.
+//
+//   U(p) = sum_s w_s(p) x(p + d_s) + inv_s [p - d_s inside] w_s(p - d_s) x(p - d_s)
+//   Z(p) = sum_s w_s(p)            + inv_s [p - d_s inside] w_s(p - d_s)
+// (reference: ops.py:157-206, shift_ops_cuda.cu:256-458).
+//
+// Work split: one thread owns one pixel and NC channels.  A channel-broadcast
+// weight (w_channels == 1) is loaded once per (pixel, shift) and applied to
+// the NC channels in registers; a per-channel weight uses NC == 1.  The
+// reference gives every output pixel its own CTA with one lane per shift and
+// a shared-memory tree; here shifts are a sequential fp32 (fp64) register
+// accumulation and adjacent lanes own adjacent pixels, so every weight load
+// of a warp is one coalesced 128-byte row segment.
+//
+// The tiled TMA kernel in accumulate_tma.cu takes over the forward when the
+// geometry allows it; this file is the general path (any W, any alignment).
+
+#include "nsc_common.cuh"
+#include "nsc_host.h"
+#include "accumulate.h"
+
+namespace nsc {
+namespace {
+
+constexpr int kBX = 32, kBY = 8;
+
+// Row addressing of x.  Full image: circular rows.  Row band: x_ext holds
+// R halo rows above and below the band, already wrapped, so no wrap.
+struct XRows {
+    int64_t H;      // rows of the x buffer
+    int64_t off;    // buffer row of output row 0
+    int wrap;       // 1: full image, circular rows
+    __device__ __forceinline__ int64_t fwd(int64_t r) const {
+        return wrap ? wrap1(r, H) : r + off;
+    }
+    __device__ __forceinline__ int64_t own(int64_t r) const {
+        return wrap ? r : r + off;
+    }
+};
+
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(kBX * kBY)
+acc_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+               typename Acc<TX>::type* __restrict__ U,
+               typename Acc<TX>::type* __restrict__ Z, const ShiftTable st,
+               int64_t B, int64_t C, int64_t Hout, int64_t W, int64_t Cw,
+               XRows xr, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= Hout) return;
+    const int64_t plane_x = xr.H * W;
+    const int64_t plane_o = Hout * W;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    for (int64_t g = blockIdx.z; g < groups; g += gridDim.z) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const TX* xb = x + (b * C + c0) * plane_x;
+        A u[NC], z = A(0);
+#pragma unroll
+        for (int i = 0; i < NC; ++i) u[i] = A(0);
+        for (int s = 0; s < st.S; ++s) {
+            const int64_t dx = st.dx[s], dy = st.dy[s];
+            const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane_o;
+            const A wv = ldg_acc<TW, A>(ws + h * W + wcol);
+            const int64_t xo = xr.fwd(h + dx) * W + wrap1(wcol + dy, W);
+#pragma unroll
+            for (int i = 0; i < NC; ++i)
+                if (i < nc) u[i] += wv * ldg_acc<TX, A>(xb + i * plane_x + xo);
+            z += wv;
+            if (st.has_inv(s)) {
+                const int64_t hm = h - dx, wm = wcol - dy;
+                if (inb(hm, Hout) && inb(wm, W)) {
+                    const A mv = ldg_acc<TW, A>(ws + hm * W + wm);
+                    const int64_t mo = xr.own(hm) * W + wm;
+#pragma unroll
+                    for (int i = 0; i < NC; ++i)
+                        if (i < nc) u[i] += mv * ldg_acc<TX, A>(xb + i * plane_x + mo);
+                    z += mv;
+                }
+            }
+        }
+        const int64_t ob = (b * C + c0) * plane_o + h * W + wcol;
+#pragma unroll
+        for (int i = 0; i < NC; ++i)
+            if (i < nc) {
+                U[ob + i * plane_o] = u[i];
+                Z[ob + i * plane_o] = z;
+            }
+    }
+}
+
+// Mirror contributions of the band's own weights to the R rows outside it.
+// edge: (2, B, C, R, W); part 0 = U, part 1 = Z.  `top` selects the rows
+// above the band (targets row0-R .. row0-1) or below it.
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(kBX * kBY)
+acc_edge_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                typename Acc<TX>::type* __restrict__ edge, const ShiftTable st,
+                int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t Cw,
+                int64_t R, int64_t row0, int64_t Hg, int top, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t e = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || e >= R) return;
+    const int64_t t = top ? (e - R) : (Hb + e);  // target row, band-local
+    const int64_t plane_x = (Hb + 2 * R) * W;
+    const int64_t plane_o = Hb * W;
+    const int64_t plane_e = R * W;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    const bool in_image = inb(row0 + t, Hg);
+    for (int64_t g = blockIdx.z; g < groups; g += gridDim.z) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const TX* xb = x + (b * C + c0) * plane_x;
+        A u[NC], z = A(0);
+#pragma unroll
+        for (int i = 0; i < NC; ++i) u[i] = A(0);
+        if (in_image) {
+            for (int s = 0; s < st.S; ++s) {
+                if (!st.has_inv(s)) continue;
+                const int64_t hm = t - st.dx[s], wm = wcol - st.dy[s];
+                if (!inb(hm, Hb) || !inb(wm, W)) continue;
+                const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane_o;
+                const A mv = ldg_acc<TW, A>(ws + hm * W + wm);
+                const int64_t mo = (hm + R) * W + wm;
+#pragma unroll
+                for (int i = 0; i < NC; ++i)
+                    if (i < nc) u[i] += mv * ldg_acc<TX, A>(xb + i * plane_x + mo);
+                z += mv;
+            }
+        }
+        const int64_t ob = (b * C + c0) * plane_e + e * W + wcol;
+        const int64_t zoff = B * C * plane_e;
+#pragma unroll
+        for (int i = 0; i < NC; ++i)
+            if (i < nc) {
+                edge[ob + i * plane_e] = u[i];
+                edge[zoff + ob + i * plane_e] = z;
+            }
+    }
+}
+
+// Fused backward: thread owns pixel q and NC channels.
+//   gx(q)   = sum_s w_s(q-d) gU(q-d) [circular] + inv [q+d inside] w_s(q) gU(q+d)
+//   gw_s(q) = sum_c x(q+d) gU(q) + gZ(q) + inv [q+d inside] (x(q) gU(q+d) + gZ(q+d))
+// One pass over the weight stack reads w once (plus the shifted re-read,
+// served by L1/L2) and writes grad_w once.
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(kBX * kBY)
+acc_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+               const typename Acc<TX>::type* __restrict__ gU,
+               const typename Acc<TX>::type* __restrict__ gZ,
+               typename Acc<TX>::type* __restrict__ gx, TW* __restrict__ gw,
+               const ShiftTable st, int64_t B, int64_t C, int64_t H,
+               int64_t W, int64_t Cw, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= H) return;
+    const int64_t plane = H * W;
+    const int64_t q = h * W + wcol;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    for (int64_t g = blockIdx.z; g < groups; g += gridDim.z) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const int64_t cb = (b * C + c0) * plane;
+        A xq[NC], acc[NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i) {
+            acc[i] = A(0);
+            xq[i] = (i < nc) ? ldg_acc<TX, A>(x + cb + i * plane + q) : A(0);
+        }
+        A gu_q[NC], gz_q = A(0);
+#pragma unroll
+        for (int i = 0; i < NC; ++i) {
+            gu_q[i] = (i < nc) ? gU[cb + i * plane + q] : A(0);
+            if (i < nc) gz_q += gZ[cb + i * plane + q];
+        }
+        for (int s = 0; s < st.S; ++s) {
+            const int64_t dx = st.dx[s], dy = st.dy[s];
+            const int64_t wbase = ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
+            const TW* ws = w + wbase;
+            // forward term of output q - d (circular) reads x(q)
+            const int64_t qs = wrap1(h - dx, H) * W + wrap1(wcol - dy, W);
+            const A w_src = ldg_acc<TW, A>(ws + qs);
+            // grad_w forward part: x(q+d) gU(q) + gZ(q)
+            const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
+            A gws = gz_q;
+#pragma unroll
+            for (int i = 0; i < NC; ++i)
+                if (i < nc) {
+                    acc[i] += w_src * gU[cb + i * plane + qs];
+                    gws += ldg_acc<TX, A>(x + cb + i * plane + qf) * gu_q[i];
+                }
+            if (st.has_inv(s) && inb(h + dx, H) && inb(wcol + dy, W)) {
+                const A w_q = ldg_acc<TW, A>(ws + q);
+                const int64_t qi = (h + dx) * W + (wcol + dy);
+#pragma unroll
+                for (int i = 0; i < NC; ++i)
+                    if (i < nc) {
+                        const A g = gU[cb + i * plane + qi];
+                        acc[i] += w_q * g;
+                        gws += xq[i] * g + gZ[cb + i * plane + qi];
+                    }
+            }
+            gw[wbase + q] = static_cast<TW>(gws);
+        }
+#pragma unroll
+        for (int i = 0; i < NC; ++i)
+            if (i < nc) gx[cb + i * plane + q] = acc[i];
+    }
+}
+
+template <int NC> struct NCTag { static constexpr int value_nc = NC; };
+
+// Dispatch helpers over (TX, TW) and NC.
+template <typename F>
+nsc_status with_types(const char* op, int xd, int wd, F&& f) {
+    if (xd == NSC_F64 && wd == NSC_F64) return f((const double*)nullptr, (const double*)nullptr);
+    if (xd == NSC_F32 && wd == NSC_F32) return f((const float*)nullptr, (const float*)nullptr);
+    if (xd == NSC_F16 && wd == NSC_F16) return f((const __half*)nullptr, (const __half*)nullptr);
+    if (xd == NSC_BF16 && wd == NSC_BF16)
+        return f((const __nv_bfloat16*)nullptr, (const __nv_bfloat16*)nullptr);
+    if (xd == NSC_F32 && wd == NSC_F16) return f((const float*)nullptr, (const __half*)nullptr);
+    if (xd == NSC_F32 && wd == NSC_BF16)
+        return f((const float*)nullptr, (const __nv_bfloat16*)nullptr);
+    return fail(NSC_ERR_UNSUPPORTED_DTYPE,
+                "%s: unsupported dtype pair (x=%d, w=%d); use equal dtypes, "
+                "fp32 x with fp16/bf16 weights, or fp64 for both", op, xd, wd);
+}
+
+template <typename F>
+void with_nc(int64_t C, int64_t Cw, F&& f) {
+    const int64_t nc = (Cw == 1) ? C : 1;
+    if (nc >= 4) f(NCTag<4>{});
+    else if (nc == 3) f(NCTag<3>{});
+    else if (nc == 2) f(NCTag<2>{});
+    else f(NCTag<1>{});
+}
+
+inline int64_t n_groups(int64_t B, int64_t C, int64_t Cw, int nc) {
+    return B * ((Cw == 1) ? (C + nc - 1) / nc : C);
+}
+
+inline dim3 grid_for(int64_t W, int64_t rows, int64_t groups) {
+    return dim3(grid_1d(W, kBX), grid_1d(rows, kBY),
+                static_cast<unsigned>(groups < 65535 ? groups : 65535));
+}
+
+nsc_status check_common(const char* op, int xd, int wd, int64_t Cw, int64_t B,
+                        int64_t C, int64_t H, int64_t W, const int64_t* shifts,
+                        int64_t S, ShiftTable* st) {
+    nsc_status e = check_extents(op, B, C, H, W);
+    if (e) return e;
+    if (acc_dtype(xd, wd) < 0)
+        return fail(NSC_ERR_UNSUPPORTED_DTYPE,
+                    "%s: unsupported dtype pair (x=%d, w=%d)", op, xd, wd);
+    if (!(Cw == C || (Cw == 1 && C >= 1)))
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: weights must be (S*B, C, H, W) or channel-broadcast "
+                    "(S*B, 1, H, W); got w_channels=%lld with C=%lld",
+                    op, (long long)Cw, (long long)C);
+    return build_shifts(op, shifts, S, 3, H, W, st);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+nsc_status acc_fwd_generic(const void* x, int xd, const void* w, int wd,
+                           int64_t Cw, int64_t B, int64_t C, int64_t Hout,
+                           int64_t W, int64_t x_rows, int64_t x_off, int wrap,
+                           const ShiftTable& st, void* U, void* Z,
+                           cudaStream_t stream) {
+    XRows xr{x_rows, x_off, wrap};
+    return with_types("accumulate_uz", xd, wd, [&](auto tx, auto tw) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        using A = typename Acc<TX>::type;
+        with_nc(C, Cw, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, Cw, NC);
+            acc_fwd_kernel<TX, TW, NC><<<grid_for(W, Hout, groups),
+                                          dim3(kBX, kBY), 0, stream>>>(
+                static_cast<const TX*>(x), static_cast<const TW*>(w),
+                static_cast<A*>(U), static_cast<A*>(Z), st, B, C, Hout, W, Cw,
+                xr, groups);
+        });
+        return check_launch("accumulate_uz");
+    });
+}
+
+
+nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
+                     int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t row0,
+                     int64_t Hg, const ShiftTable& st, void* top, void* bot,
+                     cudaStream_t stream) {
+    const int64_t R = st.R;
+    return with_types("accumulate_uz_band_edges", xd, wd, [&](auto tx, auto tw) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        using A = typename Acc<TX>::type;
+        if (R == 0) return ok();
+        with_nc(C, Cw, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, Cw, NC);
+            for (int t = 0; t < 2; ++t)
+                acc_edge_kernel<TX, TW, NC><<<grid_for(W, R, groups),
+                                               dim3(kBX, kBY), 0, stream>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<A*>(t ? top : bot), st, B, C, Hb, W, Cw, R, row0,
+                    Hg, t, groups);
+        });
+        return check_launch("accumulate_uz_band_edges");
+    });
+}
+
+nsc_status acc_bwd(const void* x, int xd, const void* w, int wd, int64_t Cw,
+                   int64_t B, int64_t C, int64_t H, int64_t W,
+                   const ShiftTable& st, const void* gU, const void* gZ,
+                   void* gx, void* gw, cudaStream_t stream) {
+    return with_types("accumulate_uz_backward", xd, wd, [&](auto tx, auto tw) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        using A = typename Acc<TX>::type;
+        with_nc(C, Cw, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, Cw, NC);
+            acc_bwd_kernel<TX, TW, NC><<<grid_for(W, H, groups), dim3(kBX, kBY),
+                                          0, stream>>>(
+                static_cast<const TX*>(x), static_cast<const TW*>(w),
+                static_cast<const A*>(gU), static_cast<const A*>(gZ),
+                static_cast<A*>(gx), static_cast<TW*>(gw), st, B, C, H, W, Cw,
+                groups);
+        });
+        return check_launch("accumulate_uz_backward");
+    });
+}
+
+}  // namespace nsc
+
+// ---------------------------------------------------------------------------
+// C entry points
+// ---------------------------------------------------------------------------
+extern "C" {
+
+nsc_status nsc_accumulate_uz_fwd(const void* x, int x_dtype, const void* w,
+                                 int w_dtype, int64_t w_channels, int64_t B,
+                                 int64_t C, int64_t H, int64_t W,
+                                 const int64_t* shifts, int64_t S, void* U,
+                                 void* Z, void* stream) {
+    using namespace nsc;
+    ShiftTable st;
+    nsc_status e = check_common("accumulate_uz", x_dtype, w_dtype, w_channels,
+                                B, C, H, W, shifts, S, &st);
+    if (e) return e;
+    if (B == 0 || C == 0 || H == 0 || W == 0) return ok();
+    if (!x || !w || !U || !Z)
+        return fail(NSC_ERR_INVALID_ARG, "accumulate_uz: NULL tensor pointer");
+    if (acc_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0, 1,
+                     st, U, Z, as_stream(stream)))
+        return check_launch("accumulate_uz");
+    return acc_fwd_generic(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0,
+                           1, st, U, Z, as_stream(stream));
+}
+
+nsc_status nsc_accumulate_uz_bwd(const void* x, int x_dtype, const void* w,
+                                 int w_dtype, int64_t w_channels, int64_t B,
+                                 int64_t C, int64_t H, int64_t W,
+                                 const int64_t* shifts, int64_t S,
+                                 const void* grad_U, const void* grad_Z,
+                                 void* grad_x, void* grad_w, void* stream) {
+    using namespace nsc;
+    ShiftTable st;
+    nsc_status e = check_common("accumulate_uz_backward", x_dtype, w_dtype,
+                                w_channels, B, C, H, W, shifts, S, &st);
+    if (e) return e;
+    if (B == 0 || C == 0 || H == 0 || W == 0) return ok();
+    if (!x || !w || !grad_U || !grad_Z || !grad_x || !grad_w)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "accumulate_uz_backward: NULL tensor pointer");
+    return acc_bwd(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, st, grad_U,
+                   grad_Z, grad_x, grad_w, as_stream(stream));
+}
+
+static nsc_status band_checks(const char* op, int64_t Hb, int64_t row0,
+                              int64_t Hg, const nsc::ShiftTable& st) {
+    using namespace nsc;
+    if (Hg < 1 || row0 < 0 || Hb < 0 || row0 + Hb > Hg)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: band rows [%lld, %lld) outside image of %lld rows", op,
+                    (long long)row0, (long long)(row0 + Hb), (long long)Hg);
+    for (int s = 0; s < st.S; ++s)
+        if (st.dx[s] > Hg || -st.dx[s] > Hg)
+            return fail(NSC_ERR_INVALID_ARG, "%s: |dx| exceeds image rows", op);
+    if (st.R > Hb)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: band of %lld rows is thinner than the radius %d", op,
+                    (long long)Hb, st.R);
+    return ok();
+}
+
+nsc_status nsc_accumulate_uz_band_fwd(const void* x_ext, int x_dtype,
+                                      const void* w, int w_dtype,
+                                      int64_t w_channels, int64_t B, int64_t C,
+                                      int64_t Hb, int64_t W, int64_t row0,
+                                      int64_t Hg, const int64_t* shifts,
+                                      int64_t S, void* U, void* Z,
+                                      void* stream) {
+    using namespace nsc;
+    ShiftTable st;
+    // dx is checked against the global height; dy against W.
+    nsc_status e = check_common("accumulate_uz_band", x_dtype, w_dtype,
+                                w_channels, B, C, Hg, W, shifts, S, &st);
+    if (e) return e;
+    e = band_checks("accumulate_uz_band", Hb, row0, Hg, st);
+    if (e) return e;
+    if (B == 0 || C == 0 || Hb == 0 || W == 0) return ok();
+    if (!x_ext || !w || !U || !Z)
+        return fail(NSC_ERR_INVALID_ARG, "accumulate_uz_band: NULL tensor pointer");
+    const int64_t R = st.R;
+    if (acc_fwd_fast(x_ext, x_dtype, w, w_dtype, w_channels, B, C, Hb, W,
+                     Hb + 2 * R, R, 0, st, U, Z, as_stream(stream)))
+        return check_launch("accumulate_uz_band");
+    return acc_fwd_generic(x_ext, x_dtype, w, w_dtype, w_channels, B, C, Hb, W,
+                           Hb + 2 * R, R, 0, st, U, Z, as_stream(stream));
+}
+
+nsc_status nsc_accumulate_uz_band_edges(const void* x_ext, int x_dtype,
+                                        const void* w, int w_dtype,
+                                        int64_t w_channels, int64_t B,
+                                        int64_t C, int64_t Hb, int64_t W,
+                                        int64_t row0, int64_t Hg,
+                                        const int64_t* shifts, int64_t S,
+                                        void* edge_top, void* edge_bot,
+                                        void* stream) {
+    using namespace nsc;
+    ShiftTable st;
+    nsc_status e = check_common("accumulate_uz_band_edges", x_dtype, w_dtype,
+                                w_channels, B, C, Hg, W, shifts, S, &st);
+    if (e) return e;
+    e = band_checks("accumulate_uz_band_edges", Hb, row0, Hg, st);
+    if (e) return e;
+    if (B == 0 || C == 0 || Hb == 0 || W == 0 || st.R == 0) return ok();
+    if (!x_ext || !w || !edge_top || !edge_bot)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "accumulate_uz_band_edges: NULL tensor pointer");
+    return acc_edges(x_ext, x_dtype, w, w_dtype, w_channels, B, C, Hb, W, row0,
+                     Hg, st, edge_top, edge_bot, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,25 @@
+// accumulate.h -- internal launchers shared by the accumulate_uz sources.
+#pragma once
+
+#include "nsc_common.cuh"
+
+namespace nsc {
+
+// General forward (any geometry).  Output rows [0, Hout); x rows are read
+// from a buffer of x_rows rows where output row 0 sits at buffer row x_off;
+// wrap != 0 means the buffer is the full image with circular rows.
+nsc_status acc_fwd_generic(const void* x, int xd, const void* w, int wd,
+                           int64_t Cw, int64_t B, int64_t C, int64_t Hout,
+                           int64_t W, int64_t x_rows, int64_t x_off, int wrap,
+                           const ShiftTable& st, void* U, void* Z,
+                           cudaStream_t stream);
+
+// Tiled fast forward.  Returns false (launching nothing) when the geometry
+// or dtypes are outside what it handles; the caller then uses the generic
+// path.
+bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
+                  int64_t B, int64_t C, int64_t Hout, int64_t W,
+                  int64_t x_rows, int64_t x_off, int wrap,
+                  const ShiftTable& st, void* U, void* Z, cudaStream_t stream);
+
+}  // namespace nsc

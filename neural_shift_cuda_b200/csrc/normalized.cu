@@ -1,0 +1,356 @@
+// normalized.cu -- normalized_accumulate_uz forward / backward.
+//
+// D(p) = sum a_i x_i / sum a_i over the keys of output p (forward term of
+// every shift plus the mirror term of has_inv rows inside the image), with
+// a_i = exp(l_i - m) for logits (log_weights) or w_i / m for positive
+// weights, m the row maximum; log_C = (m or log m) + log(sum a_i).
+// Semantics follow the reference kernels (shift_ops_cuda.cu:460-791):
+// masked keys (-inf logit, zero weight) contribute nothing; a row with no
+// live key gives D = 0, log_C = -inf; a NaN key, a negative positive weight
+// or a +inf key make D and log_C NaN.
+//
+// The reference makes two block-wide tree passes per output (max, then
+// sums).  Here one thread streams the S keys once with a running maximum:
+// whenever a key exceeds the current maximum the partial sums are rescaled
+// by exp(m_old - m_new) (w_old / w_new in positive mode), the recurrence of
+// online softmax (Milakov & Gimelshein, 2018).  A channel-broadcast weight
+// (w_channels == 1) shares one key sequence -- one exponential per key --
+// across the NC channels a thread owns.
+
+#include <cmath>
+
+#include "nsc_common.cuh"
+#include "nsc_host.h"
+
+namespace nsc {
+namespace {
+
+constexpr int kBX = 32, kBY = 8;
+
+__device__ __forceinline__ float exp_acc(float v) { return expf(v); }
+__device__ __forceinline__ double exp_acc(double v) { return exp(v); }
+__device__ __forceinline__ float log_acc(float v) { return logf(v); }
+__device__ __forceinline__ double log_acc(double v) { return log(v); }
+
+template <typename A>
+__device__ __forceinline__ A neg_inf() { return -INFINITY; }
+
+template <typename A, int NC>
+struct Online {
+    A m, sz, su[NC];
+    bool bad;
+    __device__ __forceinline__ void init() {
+        m = neg_inf<A>();
+        sz = A(0);
+        bad = false;
+#pragma unroll
+        for (int i = 0; i < NC; ++i) su[i] = A(0);
+    }
+    // k: raw weight (positive mode) or logit; xv: the key's values.
+    __device__ __forceinline__ void push(A k, const A (&xv)[NC], bool logw) {
+        if (k != k) { bad = true; return; }
+        if (logw) {
+            if (k == neg_inf<A>()) return;
+        } else {
+            if (k < A(0)) { bad = true; return; }
+            if (k == A(0)) return;
+        }
+        if (k > m) {
+            const A f = (m == neg_inf<A>()) ? A(0)
+                        : (logw ? exp_acc(m - k) : m / k);
+            sz *= f;
+#pragma unroll
+            for (int i = 0; i < NC; ++i) su[i] *= f;
+            m = k;
+        }
+        const A a = logw ? exp_acc(k - m) : k / m;
+        sz += a;
+#pragma unroll
+        for (int i = 0; i < NC; ++i) su[i] += a * xv[i];
+    }
+};
+
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(kBX * kBY)
+norm_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                typename Acc<TX>::type* __restrict__ D,
+                typename Acc<TX>::type* __restrict__ L, const ShiftTable st,
+                int64_t B, int64_t C, int64_t H, int64_t W, int64_t Cw,
+                int logw, int* __restrict__ invalid, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= H) return;
+    const int64_t plane = H * W;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    bool seen_invalid = false;
+    for (int64_t g = blockIdx.z; g < groups; g += gridDim.z) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const TX* xb = x + (b * C + c0) * plane;
+        Online<A, NC> on;
+        on.init();
+        for (int s = 0; s < st.S; ++s) {
+            const int64_t dx = st.dx[s], dy = st.dy[s];
+            const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
+            A xv[NC];
+            const int64_t xo = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
+#pragma unroll
+            for (int i = 0; i < NC; ++i)
+                xv[i] = (i < nc) ? ldg_acc<TX, A>(xb + i * plane + xo) : A(0);
+            const A kf = ldg_acc<TW, A>(ws + h * W + wcol);
+            // weight contract: finite, or -inf (logits) / >= 0 (positive)
+            if (kf != kf || kf == A(INFINITY) || (!logw && kf < A(0)))
+                seen_invalid = true;
+            on.push(kf, xv, logw);
+            if (st.has_inv(s)) {
+                const int64_t hm = h - dx, wm = wcol - dy;
+                if (inb(hm, H) && inb(wm, W)) {
+                    const int64_t mo = hm * W + wm;
+#pragma unroll
+                    for (int i = 0; i < NC; ++i)
+                        xv[i] = (i < nc) ? ldg_acc<TX, A>(xb + i * plane + mo) : A(0);
+                    on.push(ldg_acc<TW, A>(ws + mo), xv, logw);
+                }
+            }
+        }
+        const int64_t ob = (b * C + c0) * plane + h * W + wcol;
+        const A nan = A(NAN);
+#pragma unroll
+        for (int i = 0; i < NC; ++i) {
+            if (i >= nc) continue;
+            A d, l;
+            if (on.bad) {
+                d = nan; l = nan;
+            } else if (on.m == neg_inf<A>()) {
+                d = A(0); l = neg_inf<A>();
+            } else if (isfinite(on.m) && on.sz > A(0) && isfinite(on.sz)) {
+                d = on.su[i] / on.sz;
+                l = (logw ? on.m : log_acc(on.m)) + log_acc(on.sz);
+            } else {
+                d = nan; l = nan;
+            }
+            D[ob + i * plane] = d;
+            L[ob + i * plane] = l;
+        }
+    }
+    if (seen_invalid && invalid) atomicOr(invalid, 1);
+}
+
+template <typename A>
+__device__ __forceinline__ A as_log(A v, int logw) {
+    if (logw) return v;
+    if (v > A(0)) return log_acc(v);
+    if (v == A(0)) return neg_inf<A>();
+    return A(NAN);
+}
+
+template <typename A>
+__device__ __forceinline__ A fraction(A lw, A lc) {
+    if (lw == neg_inf<A>() || lc == neg_inf<A>()) return A(0);
+    return exp_acc(lw - lc);
+}
+
+// Fused backward, thread per pixel q and NC channels:
+//   gx(q)   = sum_s p(w_s(q-d), logC(q-d)) gD(q-d)  [circular]
+//           + inv [q+d inside] p(w_s(q), logC(q+d)) gD(q+d)
+//   gw_s(q) = fac(q) (gD(q) (x(q+d) - D(q)) + gL(q))
+//           + inv [q+d inside] fac'(q+d) (gD(q+d) (x(q) - D(q+d)) + gL(q+d))
+// with fac = p (log mode) or exp(-logC) (positive mode); gw = 0 for masked.
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(kBX * kBY)
+norm_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                const typename Acc<TX>::type* __restrict__ D,
+                const typename Acc<TX>::type* __restrict__ L,
+                const typename Acc<TX>::type* __restrict__ gD,
+                const typename Acc<TX>::type* __restrict__ gL,
+                typename Acc<TX>::type* __restrict__ gx, TW* __restrict__ gw,
+                const ShiftTable st, int64_t B, int64_t C, int64_t H,
+                int64_t W, int64_t Cw, int logw, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= H) return;
+    const int64_t plane = H * W;
+    const int64_t q = h * W + wcol;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    for (int64_t g = blockIdx.z; g < groups; g += gridDim.z) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const int64_t cb = (b * C + c0) * plane;
+        A acc[NC], xq[NC], Lq[NC], Dq[NC], gDq[NC], gLq[NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i) {
+            acc[i] = A(0);
+            const bool on = i < nc;
+            xq[i] = on ? ldg_acc<TX, A>(x + cb + i * plane + q) : A(0);
+            Lq[i] = on ? L[cb + i * plane + q] : A(0);
+            Dq[i] = on ? D[cb + i * plane + q] : A(0);
+            gDq[i] = on ? gD[cb + i * plane + q] : A(0);
+            gLq[i] = on ? gL[cb + i * plane + q] : A(0);
+        }
+        for (int s = 0; s < st.S; ++s) {
+            const int64_t dx = st.dx[s], dy = st.dy[s];
+            const int64_t wbase = ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
+            const TW* ws = w + wbase;
+            const int64_t qs = wrap1(h - dx, H) * W + wrap1(wcol - dy, W);
+            const A lw_src = as_log(ldg_acc<TW, A>(ws + qs), logw);
+            const A vq = ldg_acc<TW, A>(ws + q);
+            const A lw_q = as_log(vq, logw);
+            const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
+            const bool mir = st.has_inv(s) && inb(h + dx, H) && inb(wcol + dy, W);
+            const int64_t qi = (h + dx) * W + (wcol + dy);
+            A gws = A(0);
+#pragma unroll
+            for (int i = 0; i < NC; ++i) {
+                if (i >= nc) continue;
+                const int64_t co = cb + i * plane;
+                acc[i] += fraction(lw_src, L[co + qs]) * gD[co + qs];
+                const A score = gDq[i] * (ldg_acc<TX, A>(x + co + qf) - Dq[i]) + gLq[i];
+                gws += (logw ? fraction(lw_q, Lq[i]) : exp_acc(-Lq[i])) * score;
+                if (mir) {
+                    const A Li = L[co + qi];
+                    const A gDi = gD[co + qi];
+                    acc[i] += fraction(lw_q, Li) * gDi;
+                    const A score_i = gDi * (xq[i] - D[co + qi]) + gL[co + qi];
+                    gws += (logw ? fraction(lw_q, Li) : exp_acc(-Li)) * score_i;
+                }
+            }
+            if (lw_q == neg_inf<A>()) gws = A(0);
+            gw[wbase + q] = static_cast<TW>(gws);
+        }
+#pragma unroll
+        for (int i = 0; i < NC; ++i)
+            if (i < nc) gx[cb + i * plane + q] = acc[i];
+    }
+}
+
+template <int NC> struct NCTag { static constexpr int value_nc = NC; };
+
+template <typename F>
+nsc_status with_types(const char* op, int xd, int wd, F&& f) {
+    if (xd == NSC_F64 && wd == NSC_F64) return f((const double*)nullptr, (const double*)nullptr);
+    if (xd == NSC_F32 && wd == NSC_F32) return f((const float*)nullptr, (const float*)nullptr);
+    if (xd == NSC_F16 && wd == NSC_F16) return f((const __half*)nullptr, (const __half*)nullptr);
+    if (xd == NSC_BF16 && wd == NSC_BF16)
+        return f((const __nv_bfloat16*)nullptr, (const __nv_bfloat16*)nullptr);
+    if (xd == NSC_F32 && wd == NSC_F16) return f((const float*)nullptr, (const __half*)nullptr);
+    if (xd == NSC_F32 && wd == NSC_BF16)
+        return f((const float*)nullptr, (const __nv_bfloat16*)nullptr);
+    return fail(NSC_ERR_UNSUPPORTED_DTYPE,
+                "%s: unsupported dtype pair (x=%d, w=%d)", op, xd, wd);
+}
+
+template <typename F>
+void with_nc(int64_t C, int64_t Cw, F&& f) {
+    const int64_t nc = (Cw == 1) ? C : 1;
+    if (nc >= 4) f(NCTag<4>{});
+    else if (nc == 3) f(NCTag<3>{});
+    else if (nc == 2) f(NCTag<2>{});
+    else f(NCTag<1>{});
+}
+
+inline int64_t n_groups(int64_t B, int64_t C, int64_t Cw, int nc) {
+    return B * ((Cw == 1) ? (C + nc - 1) / nc : C);
+}
+
+inline dim3 grid_for(int64_t W, int64_t rows, int64_t groups) {
+    return dim3(grid_1d(W, kBX), grid_1d(rows, kBY),
+                static_cast<unsigned>(groups < 65535 ? groups : 65535));
+}
+
+nsc_status check_common(const char* op, int xd, int wd, int64_t Cw, int64_t B,
+                        int64_t C, int64_t H, int64_t W, const int64_t* shifts,
+                        int64_t S, ShiftTable* st) {
+    nsc_status e = check_extents(op, B, C, H, W);
+    if (e) return e;
+    if (acc_dtype(xd, wd) < 0)
+        return fail(NSC_ERR_UNSUPPORTED_DTYPE,
+                    "%s: unsupported dtype pair (x=%d, w=%d)", op, xd, wd);
+    if (!(Cw == C || (Cw == 1 && C >= 1)))
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: weights must be (S*B, C, H, W) or channel-broadcast "
+                    "(S*B, 1, H, W); got w_channels=%lld with C=%lld",
+                    op, (long long)Cw, (long long)C);
+    return build_shifts(op, shifts, S, 3, H, W, st);
+}
+
+}  // namespace
+}  // namespace nsc
+
+extern "C" {
+
+nsc_status nsc_normalized_accumulate_uz_fwd(
+    const void* x, int x_dtype, const void* w, int w_dtype, int64_t w_channels,
+    int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* shifts,
+    int64_t S, int log_weights, void* D, void* log_C, int* invalid_flag,
+    void* stream) {
+    using namespace nsc;
+    const char* op = "normalized_accumulate_uz";
+    ShiftTable st;
+    nsc_status e = check_common(op, x_dtype, w_dtype, w_channels, B, C, H, W,
+                                shifts, S, &st);
+    if (e) return e;
+    if (B == 0 || C == 0 || H == 0 || W == 0) return ok();
+    if (!x || !w || !D || !log_C)
+        return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
+    cudaStream_t sm = as_stream(stream);
+    return with_types(op, x_dtype, w_dtype, [&](auto tx, auto tw) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        using A = typename Acc<TX>::type;
+        with_nc(C, w_channels, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, w_channels, NC);
+            norm_fwd_kernel<TX, TW, NC><<<grid_for(W, H, groups),
+                                           dim3(kBX, kBY), 0, sm>>>(
+                static_cast<const TX*>(x), static_cast<const TW*>(w),
+                static_cast<A*>(D), static_cast<A*>(log_C), st, B, C, H, W,
+                w_channels, log_weights ? 1 : 0, invalid_flag, groups);
+        });
+        return check_launch(op);
+    });
+}
+
+nsc_status nsc_normalized_accumulate_uz_bwd(
+    const void* x, int x_dtype, const void* w, int w_dtype, int64_t w_channels,
+    int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* shifts,
+    int64_t S, int log_weights, const void* D, const void* log_C,
+    const void* grad_D, const void* grad_log_C, void* grad_x, void* grad_w,
+    void* stream) {
+    using namespace nsc;
+    const char* op = "normalized_accumulate_uz_backward";
+    ShiftTable st;
+    nsc_status e = check_common(op, x_dtype, w_dtype, w_channels, B, C, H, W,
+                                shifts, S, &st);
+    if (e) return e;
+    if (B == 0 || C == 0 || H == 0 || W == 0) return ok();
+    if (!x || !w || !D || !log_C || !grad_D || !grad_log_C || !grad_x || !grad_w)
+        return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
+    cudaStream_t sm = as_stream(stream);
+    return with_types(op, x_dtype, w_dtype, [&](auto tx, auto tw) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        using A = typename Acc<TX>::type;
+        with_nc(C, w_channels, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, w_channels, NC);
+            norm_bwd_kernel<TX, TW, NC><<<grid_for(W, H, groups),
+                                           dim3(kBX, kBY), 0, sm>>>(
+                static_cast<const TX*>(x), static_cast<const TW*>(w),
+                static_cast<const A*>(D), static_cast<const A*>(log_C),
+                static_cast<const A*>(grad_D), static_cast<const A*>(grad_log_C),
+                static_cast<A*>(grad_x), static_cast<TW*>(grad_w), st, B, C, H,
+                W, w_channels, log_weights ? 1 : 0, groups);
+        });
+        return check_launch(op);
+    });
+}
+
+}  // extern "C"
