@@ -194,6 +194,36 @@ NSC_API nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype,
                               const void* grad_d_hat, void* grad_degree,
                               void* grad_w, void* grad_img, void* stream);
 
+/* ---------------------------------------------------------------------
+ * Allocation-free metropolis forward.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory: a plugin whose host
+ * framework owns every allocation and hands it only the input and output
+ * buffers (no workspace), or code that must not call cudaMalloc because
+ * it can synchronize the device or fail in the middle of a run.  Same
+ * arguments and results as nsc_metropolis_fwd, minus `degree`: the degree
+ * map lives in a fixed scratch array inside the library instead.
+ *
+ * Limit: B * w_channels * H * W * sizeof(accumulator) must not exceed
+ * NSC_NOALLOC_SCRATCH_BYTES (16 MiB: 4,194,304 fp32 values, e.g. 16 images
+ * of 512 x 512 with channel-shared weights); larger calls fail with
+ * NSC_ERR_INVALID_ARG.  The array is static device memory, held by every
+ * GPU that loads the library until the process exits.  The first call on
+ * a device looks the array's device address up (once per device); make
+ * that first call before any stream capture.  Every call shares the one
+ * array, so calls that overlap on the GPU (other streams, other threads)
+ * race; serialize them.  The array keeps the last call's contents, which
+ * is harmless: the degree pass overwrites every value it later reads.
+ * ------------------------------------------------------------------- */
+#define NSC_NOALLOC_SCRATCH_BYTES (16u << 20)
+NSC_API nsc_status nsc_metropolis_fwd_noalloc(const void* w_half, int w_dtype,
+                                      int64_t w_channels, const void* img,
+                                      int x_dtype, int64_t B, int64_t C,
+                                      int64_t H, int64_t W,
+                                      const int64_t* shifts, int64_t S,
+                                      int use_box, double eps, void* Wx,
+                                      void* d_hat, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

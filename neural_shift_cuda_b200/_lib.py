@@ -59,6 +59,8 @@ _SIGS = {
                                          _P],
     "nsc_metropolis_fwd": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP, _L, _I,
                            _D, _P, _P, _P, _P],
+    "nsc_metropolis_fwd_noalloc": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP,
+                                   _L, _I, _D, _P, _P, _P],
     "nsc_metropolis_bwd": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP, _L, _I,
                            _D, _P, _P, _P, _P, _P, _P, _P, _P],
 }

@@ -421,3 +421,83 @@ nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype, int64_t w_channel
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free forward (no counterpart in the reference).  For callers
+// that cannot allocate device memory -- a plugin whose host framework owns
+// all allocations and passes only inputs and outputs, or code that must not
+// call cudaMalloc -- the degree map goes to this fixed file-scope array.
+// Host code never passes `g_noalloc_scratch` itself to a kernel: on the host
+// that name is only a stand-in, so its device address is looked up per
+// device with cudaGetSymbolAddress and cached.  Calls that overlap on the
+// GPU share the array and race; the degree pass overwrites every value the
+// aggregation reads, so stale contents from an earlier call do not matter.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace nsc {
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NSC_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device (set-up on the
+// first call per device).  Returns nullptr and sets the error on failure.
+void* noalloc_scratch(const char* op) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        fail(NSC_ERR_LAUNCH_FAILED, "%s: no usable current device (%s)", op,
+             cudaGetErrorString(e));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            fail(NSC_ERR_LAUNCH_FAILED,
+                 "%s: cudaGetSymbolAddress of the scratch array failed: %s", op,
+                 cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_noalloc_ptr[dev] = p;
+    }
+    return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+}  // namespace nsc
+
+extern "C" nsc_status nsc_metropolis_fwd_noalloc(
+    const void* w_half, int w_dtype, int64_t w_channels, const void* img,
+    int x_dtype, int64_t B, int64_t C, int64_t H, int64_t W,
+    const int64_t* shifts, int64_t S, int use_box, double eps, void* Wx,
+    void* d_hat, void* stream) {
+    using namespace nsc;
+    const char* op = "metropolis_aggregate_noalloc";
+    ShiftTable st;
+    nsc_status e = check_metro(op, w_channels, B, C, H, W, shifts, S, eps, &st);
+    if (e) return e;
+    if (B == 0 || C == 0 || H == 0 || W == 0) return ok();
+    if (!valid_dtype(x_dtype))
+        return fail(NSC_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype", op);
+    const double need = static_cast<double>(B) * static_cast<double>(w_channels) *
+                        static_cast<double>(H) * static_cast<double>(W) *
+                        (x_dtype == NSC_F64 ? 8.0 : 4.0);
+    if (need > static_cast<double>(NSC_NOALLOC_SCRATCH_BYTES))
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: the degree map needs %.0f bytes but the built-in "
+                    "scratch holds %u (B * w_channels * H * W * %d); use "
+                    "nsc_metropolis_fwd with a caller-allocated degree buffer",
+                    op, need, NSC_NOALLOC_SCRATCH_BYTES,
+                    x_dtype == NSC_F64 ? 8 : 4);
+    void* scratch = noalloc_scratch(op);
+    if (!scratch) return NSC_ERR_LAUNCH_FAILED;
+    return nsc_metropolis_fwd(w_half, w_dtype, w_channels, img, x_dtype, B, C,
+                              H, W, shifts, S, use_box, eps, Wx, d_hat, scratch,
+                              stream);
+}
