@@ -376,7 +376,13 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--size", type=int, default=8192,
+                    help="image side (8192 is the benchmark; smaller sides "
+                         "are for profiling captures only)")
     args = ap.parse_args()
+    global HG, WG, PIXEL_SHIFTS
+    HG = WG = args.size
+    PIXEL_SHIFTS = S * B * C * HG * WG
     if args.impl == "reference":
         run_reference(args)
     else:

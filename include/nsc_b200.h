@@ -64,6 +64,14 @@ NSC_API const char* nsc_version(void);
 /* Message of the last failed call on this host thread ("" if none). */
 NSC_API const char* nsc_last_error_string(void);
 
+/* Number of bounded device-side waits (mbarrier polls in the tiled
+ * kernels) that gave up on the current device since the library loaded;
+ * 0 in a healthy run.  A kernel whose wait gives up stops waiting and
+ * returns instead of hanging, leaving its outputs undefined.  This call
+ * synchronizes with the device (a diagnostic, not for hot loops); it
+ * returns 0xFFFFFFFF if the counter cannot be read. */
+NSC_API unsigned int nsc_wait_timeouts(void);
+
 /* ---------------------------------------------------------------------
  * Gathers.  Replace shift_gather_forward / pair_gather_forward
  * (csrc/shift_ops.cpp:81-140) and their backward (shift_ops.cpp:102-156).

@@ -18,7 +18,8 @@ from typing import Optional
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libnsc_b200.so")
+LIB_PATH = os.environ.get("NSC_LIB_PATH") or os.path.join(
+    _HERE, "_lib", "libnsc_b200.so")
 
 NSC_F16, NSC_BF16, NSC_F32, NSC_F64 = 0, 1, 2, 3
 _DTYPES = {torch.float16: NSC_F16, torch.bfloat16: NSC_BF16,
@@ -66,7 +67,7 @@ _SIGS = {
 }
 
 EXPORTED = ["nsc_index_width_bits", "nsc_version", "nsc_last_error_string",
-            *_SIGS]
+            "nsc_wait_timeouts", *_SIGS]
 
 
 def load() -> ctypes.CDLL:
@@ -82,6 +83,7 @@ def load() -> ctypes.CDLL:
             lib.nsc_index_width_bits.restype = ctypes.c_int
             lib.nsc_version.restype = ctypes.c_char_p
             lib.nsc_last_error_string.restype = ctypes.c_char_p
+            lib.nsc_wait_timeouts.restype = ctypes.c_uint
             for name, args in _SIGS.items():
                 fn = getattr(lib, name)
                 fn.argtypes = args
@@ -106,6 +108,11 @@ def available() -> bool:
 
 def index_width_bits() -> int:
     return int(load().nsc_index_width_bits())
+
+
+def wait_timeouts() -> int:
+    """Bounded device waits that gave up on the current device (synchronizes)."""
+    return int(load().nsc_wait_timeouts())
 
 
 def version() -> str:

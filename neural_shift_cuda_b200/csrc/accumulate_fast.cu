@@ -1,11 +1,171 @@
-// accumulate_fast.cu -- placeholder for the tiled forward; declines every
-// call so the generic path runs.
+// accumulate_fast.cu -- dispatch of the tiled TMA forward (accumulate_fast.cuh).
+//
+// The tiled path takes a call when: x and weights share one storage dtype
+// (fp16, bf16 or fp32); the weight is per-channel (one image channel per
+// tile) or channel-broadcast with C in {1, 3}; rows are 16-byte aligned
+// (W * sizeof(T) % 16 == 0, 16-byte aligned pointers); every |dx|, |dy| <=
+// 16 and no (dx, dy) appears twice.  Other calls use the generic kernels.
+// The dy range of the table selects a compile-time bucket: [0, K] for
+// half-plane tables (every dy >= 0), [-K, K] otherwise, K in {4, 8, 12, 16}.
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
 #include "accumulate.h"
+#include "accumulate_fast.cuh"
+#include "nsc_host.h"
 
 namespace nsc {
-bool acc_fwd_fast(const void*, int, const void*, int, int64_t, int64_t, int64_t,
-                  int64_t, int64_t, int64_t, int64_t, int, const ShiftTable&,
-                  void*, void*, cudaStream_t) {
-    return false;
+namespace fast {
+
+template <typename T, int NC, int DYMIN, int DYMAX>
+bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x,
+            void* U, void* Z,
+            const FastTable& tab, Geo g, unsigned int* timeouts,
+            cudaStream_t stream);
+
+}  // namespace fast
+
+namespace {
+
+int sm_count() {
+    static std::mutex mu;
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
 }
+
+template <typename T, int NC>
+bool by_bucket(bool half, int K, const CUtensorMap& map, const CUtensorMap& map2,
+               const void* x, void* U,
+               void* Z, const fast::FastTable& tab, const fast::Geo& g,
+               unsigned int* to, cudaStream_t st) {
+    if (half) {
+        switch (K) {
+            case 4: return fast::launch<T, NC, 0, 4>(map, map2, x, U, Z, tab, g, to, st);
+            case 8: return fast::launch<T, NC, 0, 8>(map, map2, x, U, Z, tab, g, to, st);
+            case 12: return fast::launch<T, NC, 0, 12>(map, map2, x, U, Z, tab, g, to, st);
+            default: return fast::launch<T, NC, 0, 16>(map, map2, x, U, Z, tab, g, to, st);
+        }
+    }
+    switch (K) {
+        case 4: return fast::launch<T, NC, -4, 4>(map, map2, x, U, Z, tab, g, to, st);
+        case 8: return fast::launch<T, NC, -8, 8>(map, map2, x, U, Z, tab, g, to, st);
+        default: return fast::launch<T, NC, -12, 12>(map, map2, x, U, Z, tab, g, to, st);
+    }
+}
+
+}  // namespace
+
+bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
+                  int64_t B, int64_t C, int64_t Hout, int64_t W, int64_t x_rows,
+                  int64_t x_off, int wrap, const ShiftTable& st, void* U, void* Z,
+                  cudaStream_t stream) {
+    using namespace fast;
+    if (std::getenv("NSC_DISABLE_FAST")) return false;
+    if (xd != wd || (xd != NSC_F16 && xd != NSC_BF16 && xd != NSC_F32)) return false;
+    const int es = xd == NSC_F32 ? 4 : 2;
+    const int V = 16 / es;
+    int NC;
+    if (Cw == 1 && (C == 1 || C == 3)) NC = static_cast<int>(C);
+    else if (Cw == C) NC = 1;
+    else return false;
+    if ((W * es) % 16 != 0) return false;
+    for (const void* p : {x, w, static_cast<const void*>(U), static_cast<const void*>(Z)})
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
+
+    FastTable tab;
+    std::memset(&tab, 0, sizeof(tab));
+    for (auto& row : tab.s)
+        for (auto& v : row) v = -1;
+    int dymin = 0, dymax = 0, rx = 0;
+    for (int s = 0; s < st.S; ++s) {
+        const int dx = st.dx[s], dy = st.dy[s];
+        if (dx < -MAXR || dx > MAXR || dy < -MAXR || dy > MAXR) return false;
+        int16_t& e = tab.s[dx + MAXR][dy + MAXR];
+        if (e >= 0) return false;  // duplicate (dx, dy)
+        e = static_cast<int16_t>(s | (st.has_inv(s) ? kInvBit : 0));
+        tab.row_any[dx + MAXR] = 1;
+        if (st.has_inv(s)) tab.row_inv[dx + MAXR] = 1;
+        dymin = dy < dymin ? dy : dymin;
+        dymax = dy > dymax ? dy : dymax;
+        rx = (dx < 0 ? -dx : dx) > rx ? (dx < 0 ? -dx : dx) : rx;
+    }
+    tab.Rx = rx;
+    // Pair consecutive entries of the visiting order ((dx, dy) ascending)
+    // that are consecutive weight planes (s, s+1) with the same box origin:
+    // one TMA copy then carries both planes.
+    for (int dx = -rx; dx <= rx; ++dx) {
+        int prev = -1, prev_dy = 0;
+        for (int dy = -MAXR; dy <= MAXR; ++dy) {
+            int16_t& e = tab.s[dx + MAXR][dy + MAXR];
+            if (e < 0) continue;
+            const int mo = dy > 0 ? (dy + V - 1) / V * V : 0;
+            const int pmo = prev_dy > 0 ? (prev_dy + V - 1) / V * V : 0;
+            if (prev >= 0) {
+                int16_t& pe = tab.s[dx + MAXR][prev_dy + MAXR];
+                if (!(pe & (kPairFirst | kPairSecond)) && (e & kSMask) == (pe & kSMask) + 1 &&
+                    mo == pmo) {
+                    pe = static_cast<int16_t>(pe | kPairFirst);
+                    e = static_cast<int16_t>(e | kPairSecond);
+                }
+            }
+            prev = e;
+            prev_dy = dy;
+        }
+    }
+    const bool half = dymin >= 0;
+    const int span = half ? dymax : (dymax > -dymin ? dymax : -dymin);
+    int K = span <= 4 ? 4 : span <= 8 ? 8 : span <= 12 ? 12 : 16;
+    if (!half && K > 12) return false;
+    if (!wrap && x_off < rx) return false;  // band halo thinner than |dx|
+
+    Geo g{};
+    g.B = B; g.C = C; g.H = Hout; g.W = W; g.Cw = Cw;
+    g.x_rows = x_rows; g.x_off = x_off; g.wrap = wrap;
+    const int TW = TPR * V;
+    g.tiles_x = static_cast<int32_t>((W + TW - 1) / TW);
+    g.tiles_y = static_cast<int32_t>((Hout + TH - 1) / TH);
+    g.groups = B * (Cw == 1 ? 1 : C);
+    g.ntiles = g.groups * g.tiles_y * g.tiles_x;
+    const int XC = align_up(K, V);
+    g.BH = TH + rx;
+    g.BW = TW + XC + V;
+    g.stage_tx = static_cast<uint32_t>(g.BH) * g.BW * es;
+    g.stage_stride = (g.stage_tx + 127u) & ~127u;
+    g.XH = TH + 2 * rx;
+    g.XW = TW + 2 * XC + V;
+
+    const CUtensorMapDataType dt = xd == NSC_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : xd == NSC_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    g.plane_bytes = g.stage_tx;
+    g.stage_stride = (2 * g.stage_tx + 127u) & ~127u;   // room for a pair
+    CUtensorMap map, map2;
+    const char* err = nullptr;
+    if (!encode_map_4d(&map, w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH, 1, &err) ||
+        !encode_map_4d(&map2, w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH, 2, &err))
+        return false;
+    unsigned int* to = wait_timeout_counter();
+    if (!to) return false;
+    (void)sm_count;
+    if (xd == NSC_F16)
+        return NC == 1 ? by_bucket<__half, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
+                       : by_bucket<__half, 3>(half, K, map, map2, x, U, Z, tab, g, to, stream);
+    if (xd == NSC_BF16)
+        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
+                       : by_bucket<__nv_bfloat16, 3>(half, K, map, map2, x, U, Z, tab, g, to, stream);
+    return NC == 1 ? by_bucket<float, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
+                   : by_bucket<float, 3>(half, K, map, map2, x, U, Z, tab, g, to, stream);
+}
+
+int fast_sm_count() { return sm_count(); }
+
 }  // namespace nsc

@@ -1,0 +1,495 @@
+// accumulate_fast.cuh -- tiled TMA forward of accumulate_uz for sm_100a.
+//
+// Persistent kernel, one CTA per SM, 8 consumer warps + 1 producer warp.
+// A tile is TH = 16 output rows x TW = 16*V columns (V = 16 bytes of the
+// storage type: 8 fp16/bf16 or 4 fp32 pixels per thread) of one image and
+// one weight channel (all NC image channels when the weight is
+// channel-broadcast).
+//
+// Weights.  For every shift row s the producer TMA-loads ONE box of the
+// weight plane s that covers both uses of it: the forward term reads
+// w_s(p) on the tile, the mirror term reads w_s(p - d_s) on the tile
+// shifted by -d_s.  The box is (TH + Rx) x (TW + slack) starting at
+// (h0 - max(dx, 0), w0 - align_up(max(dy, 0))), so both reads hit shared
+// memory and each weight byte leaves HBM once (the overlap with the
+// neighbouring tiles is served by L2).  Out-of-image box parts are filled
+// with zeros by TMA, which is exactly the mirror term's mask.  The boxes
+// stream through an NSTAGE-deep ring of full/empty mbarriers.
+//
+// Image.  Per tile the consumers stage two halo tiles of x in shared
+// memory: A with circular rows/columns (forward term) and B zero outside
+// the image (mirror term: never periodic).  Shifts are visited grouped by
+// dx; for one dx every thread loads a register window of its row of A
+// (and of B) once and serves every dy of the group from it with
+// compile-time register indices (dy is a template-unrolled loop), so the
+// per-shift work is one 16-byte weight load (two for the mirror) plus
+// the FMAs.  fp16 / bf16 products use the mixed-precision
+// fma.rn.f32.{f16,bf16} (exact products, fp32 accumulation) on the packed
+// halves directly; no per-element conversion is issued.
+//
+// Summation order: per output, shifts in (dx, dy) order, forward before
+// mirror, fp32 accumulation -- within the fp32 tolerance of the
+// reference's pairwise tree (ops.py:77-92).
+#pragma once
+
+// Build-time switch for throughput experiments (0 in every shipped build):
+// 1 = stream the weights without the arithmetic, 2 = arithmetic without
+// waiting for the weights.
+#ifndef NSC_FAST_EXPERIMENT
+#define NSC_FAST_EXPERIMENT 0
+#endif
+
+#include "nsc_common.cuh"
+#include "nsc_tma.cuh"
+
+namespace nsc {
+namespace fast {
+
+constexpr int TH = 16;          // output rows per tile
+constexpr int TPR = 16;         // threads per row
+constexpr int NCONS = TH * TPR; // consumer threads
+constexpr int NTHREADS = NCONS + 32;
+constexpr int MAXSTAGE = 16;     // ring depth is chosen per launch (<= this)
+constexpr int STRIP = 8;        // tile columns per raster strip
+constexpr int MAXR = 16;        // |dx|, |dy| <= MAXR on this path
+constexpr int kInvBit = 0x800;       // row has a mirror term
+constexpr int kPairFirst = 0x1000;   // shares its weight copy with the next entry
+constexpr int kPairSecond = 0x2000;  // second plane of the previous entry's copy
+constexpr int kSMask = 0x7FF;
+
+struct FastTable {
+    int16_t s[2 * MAXR + 1][2 * MAXR + 1];  // [dx+MAXR][dy+MAXR] -> s | inv, or -1
+    uint8_t row_any[2 * MAXR + 1];
+    uint8_t row_inv[2 * MAXR + 1];
+    int32_t Rx;                             // max |dx|
+};
+
+struct Geo {
+    int64_t B, C, H, W, Cw;     // H: output (= weight) rows
+    int64_t x_rows, x_off;      // x buffer rows; buffer row of output row 0
+    int32_t wrap;               // 1: x buffer is the full image, circular rows
+    int32_t tiles_x, tiles_y;
+    int64_t groups, ntiles;
+    int32_t BH, BW;             // weight box
+    uint32_t stage_tx, stage_stride;
+    int32_t XH, XW;             // x halo tile
+    int32_t nstage;             // weight ring depth
+    uint32_t plane_bytes;       // one plane of a weight box in shared memory
+};
+
+// Tile order: planes (image, weight channel) outermost, then vertical
+// strips STRIP tiles wide, row-major inside a strip.  Consecutive tiles --
+// the ones the persistent CTAs work on at the same time -- form a compact
+// block, so the weight rows one tile's box shares with its upper, lower and
+// left neighbours are fetched by concurrently running CTAs and meet in L2.
+struct TileId {
+    int64_t b, grp;
+    int h0, w0;
+};
+
+__device__ __forceinline__ TileId decode_tile(int64_t tile, const Geo& g, int TW,
+                                              int64_t cgroups) {
+    const int64_t per = static_cast<int64_t>(g.tiles_x) * g.tiles_y;
+    const int64_t grp = tile / per;
+    const int64_t t = tile - grp * per;
+    const int64_t full = static_cast<int64_t>(STRIP) * g.tiles_y;
+    const int64_t strip = t / full;
+    const int64_t r = t - strip * full;
+    const int64_t left = g.tiles_x - strip * STRIP;
+    const int64_t sw = left < STRIP ? left : STRIP;
+    const int64_t ty = r / sw;
+    const int64_t tx = strip * STRIP + (r - ty * sw);
+    TileId id;
+    id.grp = grp;
+    id.b = grp / cgroups;
+    id.h0 = static_cast<int>(ty) * TH;
+    id.w0 = static_cast<int>(tx) * TW;
+    return id;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
+__host__ __device__ constexpr int align_up(int a, int m) {
+    return a >= 0 ? (a + m - 1) / m * m : -((-a) / m * m);
+}
+__host__ __device__ constexpr int align_down(int a, int m) {
+    return a >= 0 ? a / m * m : -((-a + m - 1) / m * m);
+}
+
+template <typename T> struct Elem;
+template <> struct Elem<__half> { static constexpr int kind = 0; };
+template <> struct Elem<__nv_bfloat16> { static constexpr int kind = 1; };
+template <> struct Elem<float> { static constexpr int kind = 2; };
+
+// acc += w[WI] * x[XI] on packed 32-bit words (element indices).
+template <typename T, int WI, int XI>
+__device__ __forceinline__ void fma_e(float& acc, const uint32_t* w, const uint32_t* x) {
+    if constexpr (Elem<T>::kind == 2) {
+        acc = fmaf(__uint_as_float(w[WI]), __uint_as_float(x[XI]), acc);
+    } else {
+        const uint32_t ww = w[WI >> 1], xx = x[XI >> 1];
+        constexpr int sel = ((WI & 1) << 1) | (XI & 1);
+        if constexpr (Elem<T>::kind == 0) {
+            if constexpr (sel == 0)
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.f16 %0, a0, b0, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+            else if constexpr (sel == 1)
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.f16 %0, a0, b1, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+            else if constexpr (sel == 2)
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.f16 %0, a1, b0, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+            else
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.f16 %0, a1, b1, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+        } else {
+            if constexpr (sel == 0)
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.bf16 %0, a0, b0, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+            else if constexpr (sel == 1)
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.bf16 %0, a0, b1, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+            else if constexpr (sel == 2)
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.bf16 %0, a1, b0, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+            else
+                asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.bf16 %0, a1, b1, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
+        }
+    }
+}
+
+// acc += w[WI]
+template <typename T, int WI>
+__device__ __forceinline__ void add_e(float& acc, const uint32_t* w) {
+    if constexpr (Elem<T>::kind == 2) {
+        acc += __uint_as_float(w[WI]);
+    } else {
+        const uint32_t ww = w[WI >> 1];
+        if constexpr (Elem<T>::kind == 0) {
+            if constexpr ((WI & 1) == 0)
+                asm("{.reg .b16 a0,a1; mov.b32 {a0,a1},%1; add.f32.f16 %0, a0, %0;}" : "+f"(acc) : "r"(ww));
+            else
+                asm("{.reg .b16 a0,a1; mov.b32 {a0,a1},%1; add.f32.f16 %0, a1, %0;}" : "+f"(acc) : "r"(ww));
+        } else {
+            if constexpr ((WI & 1) == 0)
+                asm("{.reg .b16 a0,a1; mov.b32 {a0,a1},%1; add.f32.bf16 %0, a0, %0;}" : "+f"(acc) : "r"(ww));
+            else
+                asm("{.reg .b16 a0,a1; mov.b32 {a0,a1},%1; add.f32.bf16 %0, a1, %0;}" : "+f"(acc) : "r"(ww));
+        }
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void lds_words(uint32_t (&dst)[N], const void* src, int word0 = 0) {
+    static_assert(N % 4 == 0, "16-byte granules");
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k) {
+        const uint4 v = reinterpret_cast<const uint4*>(src)[k];
+        dst[word0 + 4 * k + 0] = v.x;
+        dst[word0 + 4 * k + 1] = v.y;
+        dst[word0 + 4 * k + 2] = v.z;
+        dst[word0 + 4 * k + 3] = v.w;
+    }
+}
+
+__device__ __forceinline__ int64_t pmod(int64_t a, int64_t n) {
+    int64_t r = a % n;
+    return r < 0 ? r + n : r;
+}
+
+// Compile-time loop helper: f(std::integral_constant<int, I>) for I in [0, N).
+template <int I, int N, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (I < N) {
+        f(std::integral_constant<int, I>{});
+        static_for<I + 1, N>(f);
+    }
+}
+
+template <typename T, int NC, int DYMIN, int DYMAX>
+__global__ void __launch_bounds__(NTHREADS, 1)
+acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
+                const __grid_constant__ CUtensorMap wmap2, const T* __restrict__ x,
+                float* __restrict__ U, float* __restrict__ Zo, const FastTable tab,
+                const Geo g, unsigned int* timeouts) {
+    constexpr int V = 16 / static_cast<int>(sizeof(T));
+    constexpr int EPW = 4 / static_cast<int>(sizeof(T));   // elements per word
+    constexpr int TW = TPR * V;
+    constexpr int XC = align_up(cmax(DYMAX, -DYMIN), V);
+    constexpr int FB = align_down(DYMIN, V);
+    constexpr int LF = align_up(DYMAX + V - FB, V);         // forward window
+    constexpr int MB = align_down(-DYMAX, V);
+    constexpr int LM = align_up(V - DYMIN - MB, V);         // mirror window
+    constexpr int NDY = DYMAX - DYMIN + 1;
+
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    // TMA destinations must be 128-byte aligned: align the base explicitly
+    // (the launcher reserves 128 extra bytes).
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int NSTAGE = g.nstage;
+    unsigned char* stages = smem;
+    // x tiles: two forward buffers (double-buffered prefetch) and one
+    // zero-padded mirror buffer used only by tiles that touch the border.
+    T* xa0 = reinterpret_cast<T*>(smem + NSTAGE * g.stage_stride);
+    const int xtile = NC * g.XH * g.XW;
+    T* xb = xa0 + 2 * xtile;
+    uint64_t* full = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(xb + xtile) + 15) & ~uintptr_t(15));
+    uint64_t* empty = full + NSTAGE;
+    int& abort_flag = *reinterpret_cast<int*>(empty + NSTAGE);
+
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int i = 0; i < NSTAGE; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], NCONS / 32);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const int Rx = tab.Rx;
+    const int64_t cgroups = (g.Cw == 1) ? 1 : g.C;
+
+    // ------------------------------------------------------------ producer
+    if (tid >= NCONS) {
+        if (tid != NCONS) return;
+        uint32_t it = 0;
+        int stage = 0;
+        uint32_t phase = 0;
+        bool aborted = false;
+        for (int64_t tile = blockIdx.x; tile < g.ntiles && !aborted; tile += gridDim.x) {
+            const TileId id = decode_tile(tile, g, TW, cgroups);
+            const int64_t b = id.b;
+            const int64_t wc = (g.Cw == 1) ? 0 : id.grp % cgroups;
+            const int h0 = id.h0, w0 = id.w0;
+            for (int dx = -Rx; dx <= Rx && !aborted; ++dx) {
+                if (!tab.row_any[dx + MAXR]) continue;
+                for (int dy = DYMIN; dy <= DYMAX; ++dy) {
+                    const int e = tab.s[dx + MAXR][dy + MAXR];
+                    if (e < 0 || (e & kPairSecond)) continue;
+                    const int s = e & kSMask;
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, timeouts) ||
+                        *(volatile int*)&abort_flag) {
+                        aborted = true;
+                        *(volatile int*)&abort_flag = 1;
+                        break;
+                    }
+                    const bool pair = e & kPairFirst;
+                    mbar_arrive_expect_tx(&full[stage], pair ? 2 * g.plane_bytes
+                                                             : g.plane_bytes);
+                    const int mo = dy > 0 ? align_up(dy, V) : 0;
+                    // weight plane (s, b, wc) is slice s of the (B*Cw) index
+                    // b * Cw + wc; a pair copies slices s and s + 1.
+                    tma_load_4d(stages + stage * g.stage_stride, pair ? &wmap2 : &wmap1,
+                                &full[stage], w0 - mo, h0 - (dx > 0 ? dx : 0),
+                                static_cast<int32_t>(b * g.Cw + wc), s);
+                    ++it;
+                    if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+        // Drain: the CTA must not exit with copies into its shared memory in
+        // flight.  Wait (bounded) for the last NSTAGE loads to land.
+        const uint32_t n = it < NSTAGE ? it : NSTAGE;
+        for (uint32_t j = it - n; j < it; ++j)
+            mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts);
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    const int tr = tid / TPR, tc = tid % TPR;
+    const int lane = tid & 31;
+    int stage = 0;
+    uint32_t phase = 0;
+    const int XH = g.XH, XW = g.XW, BW = g.BW;
+
+    // A consumer whose bounded wait gave up stops waiting (`dead`) but keeps
+    // executing every barrier, so no thread is left waiting for it; all
+    // consumers leave together at the next tile boundary.
+    bool dead = false;
+    const int nv = XW / V;
+    const int xtotal = NC * XH * nv;
+    const int64_t xplane = g.x_rows * g.W;
+
+    // Chunk (c, i, jv) of the x tile of a tile at (b, c0, h0, w0): 16 bytes
+    // of row r = h0 - Rx + i, columns col0 .. col0 + V.  `direct` chunks are
+    // inside the x buffer without wrapping and are copied asynchronously.
+    auto chunk = [&](int idx, int h0, int w0, int& c, int& i, int& jv, int64_t& r,
+                     int64_t& col0, int64_t& xr, bool& rv, bool& direct) {
+        c = idx / (XH * nv);
+        const int rem = idx - c * XH * nv;
+        i = rem / nv;
+        jv = rem - i * nv;
+        r = static_cast<int64_t>(h0) - Rx + i;
+        col0 = static_cast<int64_t>(w0) - XC + jv * V;
+        xr = g.wrap ? pmod(r, g.x_rows) : r + g.x_off;
+        rv = xr >= 0 && xr < g.x_rows;
+        direct = rv && (g.wrap ? (r >= 0 && r < g.x_rows) : true) && col0 >= 0 &&
+                 col0 + V <= g.W;
+    };
+    auto issue_x = [&](int64_t tile, T* dst) {
+        const TileId id = decode_tile(tile, g, TW, cgroups);
+        const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
+        for (int idx = tid; idx < xtotal; idx += NCONS) {
+            int c, i, jv;
+            int64_t r, col0, xr;
+            bool rv, direct;
+            chunk(idx, id.h0, id.w0, c, i, jv, r, col0, xr, rv, direct);
+            if (direct)
+                cp_async16(dst + (c * XH + i) * XW + jv * V,
+                           x + (id.b * g.C + c0 + c) * xplane + xr * g.W + col0);
+        }
+        cp_async_commit();
+    };
+
+    int buf = 0;
+    if (blockIdx.x < g.ntiles) issue_x(blockIdx.x, xa0);
+    for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+        const TileId id = decode_tile(tile, g, TW, cgroups);
+        const int64_t b = id.b;
+        const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
+        const int h0 = id.h0, w0 = id.w0;
+        T* xa = xa0 + buf * xtile;
+        const bool border = h0 - Rx < 0 || h0 + TH + Rx > g.H || w0 - XC < 0 ||
+                            w0 + TW + XC + V > g.W;
+
+        // ---- finish the x tiles: wait for this tile's async copies, fill
+        // the wrapped / out-of-range chunks, build the mirror tile B
+        cp_async_wait_all();
+        named_sync(1, NCONS);
+        if (*(volatile int*)&abort_flag) break;
+        if (border) {
+            for (int idx = tid; idx < xtotal; idx += NCONS) {
+                int c, i, jv;
+                int64_t r, col0, xr;
+                bool rv, direct;
+                chunk(idx, h0, w0, c, i, jv, r, col0, xr, rv, direct);
+                const T* xp = x + (b * g.C + c0 + c) * xplane;
+                const int o = (c * XH + i) * XW + jv * V;
+                const bool own = r >= 0 && r < g.H;
+                const int64_t orow = g.wrap ? r : r + g.x_off;
+                T ea[V], eb[V];
+                if (direct) {
+                    *reinterpret_cast<uint4*>(ea) = *reinterpret_cast<const uint4*>(xa + o);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < V; ++k)
+                        ea[k] = rv ? xp[xr * g.W + pmod(col0 + k, g.W)] : T(0.0f);
+                    *reinterpret_cast<uint4*>(xa + o) = *reinterpret_cast<const uint4*>(ea);
+                }
+#pragma unroll
+                for (int k = 0; k < V; ++k) {
+                    const int64_t cc = col0 + k;
+                    const bool in = own && cc >= 0 && cc < g.W;
+                    // inside the image the own pixel equals the forward one
+                    eb[k] = in ? (direct ? ea[k] : xp[orow * g.W + cc]) : T(0.0f);
+                }
+                *reinterpret_cast<uint4*>(xb + o) = *reinterpret_cast<const uint4*>(eb);
+            }
+            named_sync(1, NCONS);
+        }
+        // prefetch the next tile's x while this one computes
+        if (tile + gridDim.x < g.ntiles) issue_x(tile + gridDim.x, xa0 + (buf ^ 1) * xtile);
+        const T* xmsrc = border ? xb : xa;
+
+        float u[NC][V], z[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            z[i] = 0.f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) u[c][i] = 0.f;
+        }
+
+        for (int dx = -Rx; dx <= Rx; ++dx) {
+            if (!tab.row_any[dx + MAXR]) continue;
+            uint32_t xf[NC][LF / EPW], xm[NC][LM / EPW];
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                lds_words(xf[c], xa + (c * XH + tr + dx + Rx) * XW + tc * V + XC + FB);
+            const bool rinv = tab.row_inv[dx + MAXR];
+            if (rinv) {
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    lds_words(xm[c], xmsrc + (c * XH + tr - dx + Rx) * XW + tc * V + XC + MB);
+            }
+            const int mrow0 = tr + (dx > 0 ? dx : 0);
+            static_for<0, NDY>([&](auto jc) {
+                constexpr int dy = DYMIN + decltype(jc)::value;
+                const int e = tab.s[dx + MAXR][dy + MAXR];
+                if (e < 0) return;
+                const bool second = e & kPairSecond;
+                if (NSC_FAST_EXPERIMENT != 2 && !second && !dead &&
+                    !mbar_wait(&full[stage], phase, timeouts)) {
+                    dead = true;
+                    *(volatile int*)&abort_flag = 1;
+                }
+                const T* st = reinterpret_cast<const T*>(
+                    stages + stage * g.stage_stride + (second ? g.plane_bytes : 0u));
+                constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
+                uint32_t wv[V / EPW];
+                lds_words(wv, st + mrow0 * BW + tc * V + mo);
+                if constexpr (NSC_FAST_EXPERIMENT == 1) {
+                    z[0] += __uint_as_float(wv[0] ^ wv[1] ^ wv[2] ^ wv[3]);
+                } else {
+                static_for<0, V>([&](auto ic) {
+                    constexpr int i = decltype(ic)::value;
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) fma_e<T, i, dy - FB + i>(u[c][i], wv, xf[c]);
+                    add_e<T, i>(z[i], wv);
+                });
+                }
+                if (NSC_FAST_EXPERIMENT != 1 && (e & kInvBit)) {
+                    constexpr int moff = mo - dy;               // >= 0
+                    constexpr int kk = moff % V;
+                    constexpr int mb = moff - kk;
+                    uint32_t mw[2 * V / EPW];
+                    lds_words<V / EPW>(*reinterpret_cast<uint32_t(*)[V / EPW]>(mw),
+                                       st + (mrow0 - dx) * BW + tc * V + mb);
+                    if constexpr (kk != 0)
+                        lds_words<V / EPW>(*reinterpret_cast<uint32_t(*)[V / EPW]>(mw + V / EPW),
+                                           st + (mrow0 - dx) * BW + tc * V + mb + V);
+                    static_for<0, V>([&](auto ic) {
+                        constexpr int i = decltype(ic)::value;
+#pragma unroll
+                        for (int c = 0; c < NC; ++c)
+                            fma_e<T, kk + i, -dy - MB + i>(u[c][i], mw, xm[c]);
+                        add_e<T, kk + i>(z[i], mw);
+                    });
+                }
+                if (!(e & kPairFirst)) {   // copy fully used: release it
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[stage]);
+                    if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+                }
+            });
+        }
+        // ---- store
+        const int64_t h = h0 + tr;
+        const int64_t wcol = w0 + tc * V;
+        if (h < g.H && wcol < g.W) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int64_t o = ((b * g.C + c0 + c) * g.H + h) * g.W + wcol;
+#pragma unroll
+                for (int q = 0; q < V / 4; ++q) {
+                    *reinterpret_cast<float4*>(U + o + 4 * q) =
+                        make_float4(u[c][4 * q], u[c][4 * q + 1], u[c][4 * q + 2], u[c][4 * q + 3]);
+                    *reinterpret_cast<float4*>(Zo + o + 4 * q) =
+                        make_float4(z[4 * q], z[4 * q + 1], z[4 * q + 2], z[4 * q + 3]);
+                }
+            }
+        }
+        buf ^= 1;
+    }
+    cp_async_wait_all();
+}
+
+}  // namespace fast
+}  // namespace nsc

@@ -1,0 +1,5 @@
+// Instantiations of the tiled accumulate_uz forward for float, NC = 3.
+#include "accumulate_fast_launch.cuh"
+using nsc::fast::FastTable;
+using nsc::fast::Geo;
+NSC_FAST_INSTANTIATE(float, 3)

@@ -1,0 +1,57 @@
+// accumulate_fast_launch.cuh -- host launcher of the tiled forward; included
+// by the per-dtype instantiation files so the kernels compile in parallel.
+#pragma once
+
+#include "accumulate_fast.cuh"
+
+namespace nsc {
+int fast_sm_count();
+
+namespace fast {
+
+template <typename T, int NC, int DYMIN, int DYMAX>
+bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, void* U, void* Z,
+            const FastTable& tab, Geo g, unsigned int* timeouts,
+            cudaStream_t stream) {
+    // ring depth: as many weight stages (<= 12) as fit next to the three
+    // x tiles in the 227 KB a CTA may use
+    const size_t fixed = 3ull * NC * g.XH * g.XW * sizeof(T) + 16 + 16 + 128;
+    const size_t per_stage = g.stage_stride + 2 * sizeof(uint64_t);
+    const size_t cap = 227u * 1024u;
+    if (fixed + 3 * per_stage > cap) return false;
+    size_t ns = (cap - fixed) / per_stage;
+    if (ns > 12) ns = 12;
+    g.nstage = static_cast<int32_t>(ns);
+    const size_t smem = fixed + ns * per_stage;
+    auto k = acc_fast_kernel<T, NC, DYMIN, DYMAX>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const int64_t nsm = fast_sm_count();
+    const unsigned grid = static_cast<unsigned>(g.ntiles < nsm ? g.ntiles : nsm);
+    k<<<grid, NTHREADS, smem, stream>>>(map1, map2, static_cast<const T*>(x),
+                                        static_cast<float*>(U),
+                                        static_cast<float*>(Z), tab, g, timeouts);
+    return true;
+}
+
+}  // namespace fast
+}  // namespace nsc
+
+#define NSC_FAST_INSTANTIATE(T, NC)                                                  \
+    template bool nsc::fast::launch<T, NC, 0, 4>(const CUtensorMap&, const CUtensorMap&, const void*,    \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
+    template bool nsc::fast::launch<T, NC, 0, 8>(const CUtensorMap&, const CUtensorMap&, const void*,    \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
+    template bool nsc::fast::launch<T, NC, 0, 12>(const CUtensorMap&, const CUtensorMap&, const void*,   \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
+    template bool nsc::fast::launch<T, NC, 0, 16>(const CUtensorMap&, const CUtensorMap&, const void*,   \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
+    template bool nsc::fast::launch<T, NC, -4, 4>(const CUtensorMap&, const CUtensorMap&, const void*,   \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
+    template bool nsc::fast::launch<T, NC, -8, 8>(const CUtensorMap&, const CUtensorMap&, const void*,   \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
+    template bool nsc::fast::launch<T, NC, -12, 12>(const CUtensorMap&, const CUtensorMap&, const void*, \
+        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);

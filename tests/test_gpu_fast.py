@@ -1,0 +1,145 @@
+"""GPU parity of the tiled TMA forward of accumulate_uz (accumulate_fast.cu)
+against the CPU oracle and against the generic kernel, including partial
+tiles, both dy buckets, all three storage dtypes, band mode, and a
+full-size (8192 x 8192, S = 221) property check.  fp32 tolerance 1e-5."""
+
+import os
+
+import pytest
+import torch
+
+import neural_shift_cuda_b200 as nsc
+from neural_shift_cuda_b200 import _lib, bands
+from oracle import nsc_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def T(rows):
+    return torch.tensor(rows, dtype=torch.int64)
+
+
+def _generic(fn, *a, **k):
+    os.environ["NSC_DISABLE_FAST"] = "1"
+    try:
+        return fn(*a, **k)
+    finally:
+        del os.environ["NSC_DISABLE_FAST"]
+
+
+def _w(S, B, Cw, H, W, sh, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.nn.functional.softplus(torch.randn(S * B, Cw, H, W, generator=g))
+    return O.premasked_weights(w, sh, B).to(dtype)
+
+
+CASES = [
+    # (B, C, Cw, H, W, table, R, dtype)
+    (1, 3, 1, 64, 256, "half", 10, torch.float16),
+    (2, 3, 1, 37, 136, "half", 3, torch.bfloat16),
+    (1, 1, 1, 50, 72, "half", 5, torch.float32),
+    (2, 2, 2, 33, 20, "window", 2, torch.float32),
+    (1, 3, 3, 40, 64, "window", 4, torch.float16),
+    (1, 3, 1, 19, 48, "window", 7, torch.bfloat16),
+    (1, 1, 1, 24, 16, "half", 12, torch.float32),
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_fast_matches_oracle_and_generic(cuda, case):
+    B, C, Cw, H, W, table, R, dt = case
+    rows = O.halfplane_shifts(R) if table == "half" else O.window_shifts(R)
+    sh = T(rows)
+    g = torch.Generator().manual_seed(1)
+    x = torch.rand(B, C, H, W, generator=g).to(dt)
+    w = _w(len(rows), B, Cw, H, W, sh, dt, 2)
+    U, Z = nsc.accumulate_uz(x.to(cuda), w.to(cuda), sh)
+    Ug, Zg = _generic(nsc.accumulate_uz, x.to(cuda), w.to(cuda), sh)
+    Ur, Zr = O.accumulate_uz(x, w.expand(-1, C, -1, -1) if Cw == 1 else w, sh)
+    torch.testing.assert_close(U.cpu(), Ur, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(Z.cpu(), Zr, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(U, Ug, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(Z, Zg, rtol=1e-5, atol=1e-5)
+    assert _lib.wait_timeouts() == 0
+
+
+def test_fast_nonfinite_x_stays_out_of_masked_mirror(cuda):
+    """The mirror term never reads outside the image: an inf in x must not
+    leak into outputs through a masked (zero) mirror weight."""
+    B, C, H, W, R = 1, 1, 32, 64, 3
+    rows = O.halfplane_shifts(R)
+    sh = T(rows)
+    x = torch.rand(B, C, H, W)
+    x[0, 0, 0, 5] = float("inf")
+    w = _w(len(rows), B, C, H, W, sh, torch.float32, 3)
+    U, Z = nsc.accumulate_uz(x.to(cuda), w.to(cuda), sh)
+    Ug, Zg = _generic(nsc.accumulate_uz, x.to(cuda), w.to(cuda), sh)
+    assert torch.equal(torch.isinf(U), torch.isinf(Ug))
+    fin = torch.isfinite(Ug)
+    torch.testing.assert_close(U[fin], Ug[fin], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("nb", [2, 4])
+def test_fast_band_split(cuda, nb):
+    B, C, H, W, R = 1, 3, 96, 128, 4
+    rows = O.halfplane_shifts(R)
+    sh = T(rows)
+    x = torch.rand(B, C, H, W, device=cuda).half()
+    w = _w(len(rows), B, 1, H, W, sh, torch.float16, 4).to(cuda)
+    U, Z = nsc.accumulate_uz(x, w, sh)
+    Ub, Zb = bands.accumulate_uz_banded_local(x, w, sh, nb)
+    torch.testing.assert_close(Ub, U, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(Zb, Z, rtol=1e-5, atol=1e-5)
+
+
+def test_fullsize_config5_properties(cuda):
+    """BASELINE configs[4] at full size: x fp16 (1,3,8192,8192), R=10
+    (S=221), channel-shared fp16 weights.  With x = 1 every product is the
+    weight itself, so U == Z bit for bit (same order, same roundings); a
+    1-strip crop checked against the oracle pins the values."""
+    H = W = 8192
+    R = 10
+    rows = O.halfplane_shifts(R)
+    S = len(rows)
+    sh = T(rows)
+    free, _ = torch.cuda.mem_get_info()
+    if free < 40e9:
+        pytest.skip("needs ~40 GB of free device memory")
+    w = torch.empty(S, 1, H, W, dtype=torch.float16, device=cuda)
+    gen = torch.Generator(device=cuda).manual_seed(0)
+    r_idx = torch.arange(H, device=cuda)
+    for s, (dx, dy, _) in enumerate(rows):
+        p = torch.nn.functional.softplus(
+            torch.randn(H, W, generator=gen, device=cuda))
+        m = (((r_idx + dx >= 0) & (r_idx + dx < H))[:, None]
+             & ((r_idx + dy >= 0) & (r_idx + dy < W))[None, :])
+        w[s, 0] = (p * m).half()
+        del p, m
+    ones = torch.ones(1, 3, H, W, dtype=torch.float16, device=cuda)
+    U, Z = nsc.accumulate_uz(ones, w, sh)
+    assert torch.equal(U, Z)
+    assert torch.isfinite(Z).all()
+    del U, Z
+    x = torch.rand(1, 3, H, W, generator=gen, device=cuda).half()
+    U, Z = nsc.accumulate_uz(x, w, sh)
+    # oracle on the 48 x 48 corner block (its result is exact for rows and
+    # columns >= R from the crop edge; the corner also exercises the image
+    # border: circular x and masked mirror terms)
+    hh = 48
+    xc = x[:, :, :hh, :hh].float().cpu()
+    wc = w[:, :, :hh, :hh].float().cpu()
+    # circular x of the full image: wrap the crop with the image's last rows
+    # and columns so the oracle sees the same neighbours.
+    xfull_rows = torch.cat([x[:, :, -R:, :].float().cpu(),
+                            x[:, :, :hh + R, :].float().cpu()], 2)
+    xwin = torch.cat([xfull_rows[..., -R:], xfull_rows[..., :hh + R]], 3)
+    wpad = torch.zeros(S, 1, hh + 2 * R, hh + 2 * R)
+    wpad[:, :, R:, R:] = w[:, :, :hh + R, :hh + R].float().cpu()
+    Uo, Zo = O.accumulate_uz(xwin, wpad.expand(-1, 3, -1, -1), sh)
+    inner = (slice(None), slice(None), slice(R, hh), slice(R, hh))
+    torch.testing.assert_close(U[:, :, :hh - R, :hh - R].cpu(), Uo[inner],
+                               rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(Z[:, :, :hh - R, :hh - R].cpu(), Zo[inner],
+                               rtol=1e-5, atol=1e-4)
+    del xc, wc
+    assert _lib.wait_timeouts() == 0
