@@ -16,6 +16,8 @@
 // The tiled TMA kernel in accumulate_tma.cu takes over the forward when the
 // geometry allows it; this file is the general path (any W, any alignment).
 
+#include <cstdlib>
+
 #include "nsc_common.cuh"
 #include "nsc_host.h"
 #include "accumulate.h"
@@ -370,6 +372,10 @@ nsc_status nsc_accumulate_uz_fwd(const void* x, int x_dtype, const void* w,
     if (acc_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0, 1,
                      st, U, Z, as_stream(stream)))
         return check_launch("accumulate_uz");
+    if (std::getenv("NSC_REQUIRE_FAST"))
+        return fail(NSC_ERR_INVALID_ARG,
+                    "accumulate_uz: the tiled path declined this call "
+                    "(NSC_REQUIRE_FAST is set): %s", fast_decline_reason());
     return acc_fwd_generic(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0,
                            1, st, U, Z, as_stream(stream));
 }

@@ -22,4 +22,7 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                   int64_t x_rows, int64_t x_off, int wrap,
                   const ShiftTable& st, void* U, void* Z, cudaStream_t stream);
 
+// Why the last acc_fwd_fast call on this thread declined ("" if it ran).
+const char* fast_decline_reason();
+
 }  // namespace nsc

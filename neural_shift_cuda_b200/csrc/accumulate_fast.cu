@@ -6,7 +6,8 @@
 // (W * sizeof(T) % 16 == 0, 16-byte aligned pointers); every |dx|, |dy| <=
 // 16 and no (dx, dy) appears twice.  Other calls use the generic kernels.
 // The dy range of the table selects a compile-time bucket: [0, K] for
-// half-plane tables (every dy >= 0), [-K, K] otherwise, K in {4, 8, 12, 16}.
+// half-plane tables (every dy >= 0, K even up to 12, or 16), [-K, K]
+// otherwise (K in {4, 8, 12}).
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -28,6 +29,9 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x,
 
 namespace {
 
+thread_local const char* g_decline = "";
+#define DECLINE(msg) do { g_decline = msg; return false; } while (0)
+
 int sm_count() {
     static std::mutex mu;
     static int cache[64] = {};
@@ -44,22 +48,26 @@ int sm_count() {
 
 template <typename T, int NC>
 bool by_bucket(bool half, int K, const CUtensorMap& map, const CUtensorMap& map2,
-               const void* x, void* U,
-               void* Z, const fast::FastTable& tab, const fast::Geo& g,
-               unsigned int* to, cudaStream_t st) {
+               const void* x, void* U, void* Z, const fast::FastTable& tab,
+               const fast::Geo& g, unsigned int* to, cudaStream_t st) {
+#define NSC_B(A, B) return fast::launch<T, NC, A, B>(map, map2, x, U, Z, tab, g, to, st)
     if (half) {
         switch (K) {
-            case 4: return fast::launch<T, NC, 0, 4>(map, map2, x, U, Z, tab, g, to, st);
-            case 8: return fast::launch<T, NC, 0, 8>(map, map2, x, U, Z, tab, g, to, st);
-            case 12: return fast::launch<T, NC, 0, 12>(map, map2, x, U, Z, tab, g, to, st);
-            default: return fast::launch<T, NC, 0, 16>(map, map2, x, U, Z, tab, g, to, st);
+            case 2: NSC_B(0, 2);
+            case 4: NSC_B(0, 4);
+            case 6: NSC_B(0, 6);
+            case 8: NSC_B(0, 8);
+            case 10: NSC_B(0, 10);
+            case 12: NSC_B(0, 12);
+            default: NSC_B(0, 16);
         }
     }
     switch (K) {
-        case 4: return fast::launch<T, NC, -4, 4>(map, map2, x, U, Z, tab, g, to, st);
-        case 8: return fast::launch<T, NC, -8, 8>(map, map2, x, U, Z, tab, g, to, st);
-        default: return fast::launch<T, NC, -12, 12>(map, map2, x, U, Z, tab, g, to, st);
+        case 4: NSC_B(-4, 4);
+        case 8: NSC_B(-8, 8);
+        default: NSC_B(-12, 12);
     }
+#undef NSC_B
 }
 
 }  // namespace
@@ -69,17 +77,18 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                   int64_t x_off, int wrap, const ShiftTable& st, void* U, void* Z,
                   cudaStream_t stream) {
     using namespace fast;
-    if (std::getenv("NSC_DISABLE_FAST")) return false;
-    if (xd != wd || (xd != NSC_F16 && xd != NSC_BF16 && xd != NSC_F32)) return false;
+    g_decline = "";
+    if (std::getenv("NSC_DISABLE_FAST")) DECLINE("disabled by NSC_DISABLE_FAST");
+    if (xd != wd || (xd != NSC_F16 && xd != NSC_BF16 && xd != NSC_F32)) DECLINE("dtype");
     const int es = xd == NSC_F32 ? 4 : 2;
     const int V = 16 / es;
     int NC;
     if (Cw == 1 && (C == 1 || C == 3)) NC = static_cast<int>(C);
     else if (Cw == C) NC = 1;
-    else return false;
-    if ((W * es) % 16 != 0) return false;
+    else DECLINE("channels");
+    if ((W * es) % 16 != 0) DECLINE("row alignment");
     for (const void* p : {x, w, static_cast<const void*>(U), static_cast<const void*>(Z)})
-        if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0) DECLINE("pointer alignment");
 
     FastTable tab;
     std::memset(&tab, 0, sizeof(tab));
@@ -88,9 +97,9 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     int dymin = 0, dymax = 0, rx = 0;
     for (int s = 0; s < st.S; ++s) {
         const int dx = st.dx[s], dy = st.dy[s];
-        if (dx < -MAXR || dx > MAXR || dy < -MAXR || dy > MAXR) return false;
+        if (dx < -MAXR || dx > MAXR || dy < -MAXR || dy > MAXR) DECLINE("radius");
         int16_t& e = tab.s[dx + MAXR][dy + MAXR];
-        if (e >= 0) return false;  // duplicate (dx, dy)
+        if (e >= 0) DECLINE("duplicate shift");
         e = static_cast<int16_t>(s | (st.has_inv(s) ? kInvBit : 0));
         tab.row_any[dx + MAXR] = 1;
         if (st.has_inv(s)) tab.row_inv[dx + MAXR] = 1;
@@ -123,9 +132,15 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     }
     const bool half = dymin >= 0;
     const int span = half ? dymax : (dymax > -dymin ? dymax : -dymin);
-    int K = span <= 4 ? 4 : span <= 8 ? 8 : span <= 12 ? 12 : 16;
-    if (!half && K > 12) return false;
-    if (!wrap && x_off < rx) return false;  // band halo thinner than |dx|
+    int K;
+    if (half) {
+        K = span <= 12 ? (span + 1) / 2 * 2 : 16;
+        if (K < 2) K = 2;
+    } else {
+        K = span <= 4 ? 4 : span <= 8 ? 8 : span <= 12 ? 12 : 16;
+        if (K > 12) DECLINE("dy range");
+    }
+    if (!wrap && x_off < rx) DECLINE("band halo");
 
     Geo g{};
     g.B = B; g.C = C; g.H = Hout; g.W = W; g.Cw = Cw;
@@ -137,11 +152,11 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     g.ntiles = g.groups * g.tiles_y * g.tiles_x;
     const int XC = align_up(K, V);
     g.BH = TH + rx;
-    g.BW = TW + XC + V;
+    g.BW = TW + XC;
     g.stage_tx = static_cast<uint32_t>(g.BH) * g.BW * es;
     g.stage_stride = (g.stage_tx + 127u) & ~127u;
     g.XH = TH + 2 * rx;
-    g.XW = TW + 2 * XC + V;
+    g.XW = TW + 2 * XC;
 
     const CUtensorMapDataType dt = xd == NSC_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                    : xd == NSC_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -152,9 +167,9 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     const char* err = nullptr;
     if (!encode_map_4d(&map, w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH, 1, &err) ||
         !encode_map_4d(&map2, w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH, 2, &err))
-        return false;
+        DECLINE("tensor map");
     unsigned int* to = wait_timeout_counter();
-    if (!to) return false;
+    if (!to) DECLINE("timeout counter");
     (void)sm_count;
     if (xd == NSC_F16)
         return NC == 1 ? by_bucket<__half, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
@@ -167,5 +182,8 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
 }
 
 int fast_sm_count() { return sm_count(); }
+
+const char* fast_decline_reason() { return g_decline; }
+void fast_set_decline(const char* why) { g_decline = why; }
 
 }  // namespace nsc

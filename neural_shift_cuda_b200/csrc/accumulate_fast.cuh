@@ -1,10 +1,10 @@
 // accumulate_fast.cuh -- tiled TMA forward of accumulate_uz for sm_100a.
 //
-// Persistent kernel, one CTA per SM, 8 consumer warps + 1 producer warp.
-// A tile is TH = 16 output rows x TW = 16*V columns (V = 16 bytes of the
-// storage type: 8 fp16/bf16 or 4 fp32 pixels per thread) of one image and
-// one weight channel (all NC image channels when the weight is
-// channel-broadcast).
+// Persistent kernel, one CTA per SM, 15 consumer warps + 1 producer warp.
+// A tile is TH = 30 output rows x TW = 16*V columns (V = 16 bytes of the
+// storage type: 8 fp16/bf16 or 4 fp32 pixels per thread, one row per
+// thread) of one image and one weight channel (all NC image channels when
+// the weight is channel-broadcast).
 //
 // Weights.  For every shift row s the producer TMA-loads ONE box of the
 // weight plane s that covers both uses of it: the forward term reads
@@ -16,12 +16,14 @@
 // with zeros by TMA, which is exactly the mirror term's mask.  The boxes
 // stream through an NSTAGE-deep ring of full/empty mbarriers.
 //
-// Image.  Per tile the consumers stage two halo tiles of x in shared
-// memory: A with circular rows/columns (forward term) and B zero outside
-// the image (mirror term: never periodic).  Shifts are visited grouped by
-// dx; for one dx every thread loads a register window of its row of A
-// (and of B) once and serves every dy of the group from it with
-// compile-time register indices (dy is a template-unrolled loop), so the
+// Image.  Per tile the consumers stage a halo tile of x with circular
+// rows/columns in shared memory (double-buffered: the next tile's copy is
+// issued with cp.async while this one computes).  Shifts are visited grouped
+// by dx; for one dx every thread loads register windows of its forward row
+// (h + dx) and mirror row (h - dx) once and serves every dy of the group with
+// compile-time register indices (dy is a template-unrolled loop); on tiles
+// touching the border the mirror window is zeroed outside the image in
+// registers (the mirror term is never periodic).  So the
 // per-shift work is one 16-byte weight load (two for the mirror) plus
 // the FMAs.  fp16 / bf16 products use the mixed-precision
 // fma.rn.f32.{f16,bf16} (exact products, fp32 accumulation) on the packed
@@ -45,7 +47,9 @@
 namespace nsc {
 namespace fast {
 
-constexpr int TH = 16;          // output rows per tile
+// 15 consumer warps + 1 producer warp = 16 warps: four per register-file
+// sub-partition, so every thread may hold up to 128 registers.
+constexpr int TH = 30;          // output rows per tile
 constexpr int TPR = 16;         // threads per row
 constexpr int NCONS = TH * TPR; // consumer threads
 constexpr int NTHREADS = NCONS + 32;
@@ -73,6 +77,7 @@ struct Geo {
     int32_t BH, BW;             // weight box
     uint32_t stage_tx, stage_stride;
     int32_t XH, XW;             // x halo tile
+    int32_t col_border;         // W is not a multiple of the tile width
     int32_t nstage;             // weight ring depth
     uint32_t plane_bytes;       // one plane of a weight box in shared memory
 };
@@ -210,6 +215,26 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
+// Load words [K, HI) of a shared-memory row into d[K - LO ...], using the
+// widest aligned vector (the row base is 16-byte aligned).
+template <int K, int HI, int LO, int N>
+__device__ __forceinline__ void load_win(uint32_t (&d)[N], const uint32_t* p) {
+    if constexpr (K < HI) {
+        if constexpr (K % 4 == 0 && K + 4 <= HI) {
+            const uint4 v = *reinterpret_cast<const uint4*>(p + K);
+            d[K - LO] = v.x; d[K - LO + 1] = v.y; d[K - LO + 2] = v.z; d[K - LO + 3] = v.w;
+            load_win<K + 4, HI, LO>(d, p);
+        } else if constexpr (K % 2 == 0 && K + 2 <= HI) {
+            const uint2 v = *reinterpret_cast<const uint2*>(p + K);
+            d[K - LO] = v.x; d[K - LO + 1] = v.y;
+            load_win<K + 2, HI, LO>(d, p);
+        } else {
+            d[K - LO] = p[K];
+            load_win<K + 1, HI, LO>(d, p);
+        }
+    }
+}
+
 template <typename T, int NC, int DYMIN, int DYMAX>
 __global__ void __launch_bounds__(NTHREADS, 1)
 acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
@@ -220,10 +245,12 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
     constexpr int EPW = 4 / static_cast<int>(sizeof(T));   // elements per word
     constexpr int TW = TPR * V;
     constexpr int XC = align_up(cmax(DYMAX, -DYMIN), V);
-    constexpr int FB = align_down(DYMIN, V);
-    constexpr int LF = align_up(DYMAX + V - FB, V);         // forward window
-    constexpr int MB = align_down(-DYMAX, V);
-    constexpr int LM = align_up(V - DYMIN - MB, V);         // mirror window
+    // register windows, in elements relative to the thread's first column
+    // (tile column tc*V), then in 32-bit words
+    constexpr int FLO = XC + DYMIN, FHI = XC + DYMAX + V;
+    constexpr int MLO = XC - DYMAX, MHI = XC - DYMIN + V;
+    constexpr int FWL = FLO / EPW, FWH = (FHI + EPW - 1) / EPW;
+    constexpr int MWL = MLO / EPW, MWH = (MHI + EPW - 1) / EPW;
     constexpr int NDY = DYMAX - DYMIN + 1;
 
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -233,13 +260,10 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int NSTAGE = g.nstage;
     unsigned char* stages = smem;
-    // x tiles: two forward buffers (double-buffered prefetch) and one
-    // zero-padded mirror buffer used only by tiles that touch the border.
     T* xa0 = reinterpret_cast<T*>(smem + NSTAGE * g.stage_stride);
     const int xtile = NC * g.XH * g.XW;
-    T* xb = xa0 + 2 * xtile;
     uint64_t* full = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(xb + xtile) + 15) & ~uintptr_t(15));
+        (reinterpret_cast<uintptr_t>(xa0 + 2 * xtile) + 15) & ~uintptr_t(15));
     uint64_t* empty = full + NSTAGE;
     int& abort_flag = *reinterpret_cast<int*>(empty + NSTAGE);
 
@@ -297,7 +321,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         }
         // Drain: the CTA must not exit with copies into its shared memory in
         // flight.  Wait (bounded) for the last NSTAGE loads to land.
-        const uint32_t n = it < NSTAGE ? it : NSTAGE;
+        const uint32_t n = it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE;
         for (uint32_t j = it - n; j < it; ++j)
             mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts);
         return;
@@ -357,47 +381,33 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
         const int h0 = id.h0, w0 = id.w0;
         T* xa = xa0 + buf * xtile;
-        const bool border = h0 - Rx < 0 || h0 + TH + Rx > g.H || w0 - XC < 0 ||
-                            w0 + TW + XC + V > g.W;
+        const bool row_border = h0 - Rx < 0 || h0 + TH + Rx > g.H;
+        const bool col_border = w0 - XC < 0 || w0 + TW + XC + V > g.W;
 
-        // ---- finish the x tiles: wait for this tile's async copies, fill
-        // the wrapped / out-of-range chunks, build the mirror tile B
+        // ---- finish the x tile: wait for this tile's async copies and fill
+        // the chunks that wrap or fall outside the x buffer
         cp_async_wait_all();
         named_sync(1, NCONS);
         if (*(volatile int*)&abort_flag) break;
-        if (border) {
+        if (row_border || col_border) {
             for (int idx = tid; idx < xtotal; idx += NCONS) {
                 int c, i, jv;
                 int64_t r, col0, xr;
                 bool rv, direct;
                 chunk(idx, h0, w0, c, i, jv, r, col0, xr, rv, direct);
+                if (direct) continue;
                 const T* xp = x + (b * g.C + c0 + c) * xplane;
-                const int o = (c * XH + i) * XW + jv * V;
-                const bool own = r >= 0 && r < g.H;
-                const int64_t orow = g.wrap ? r : r + g.x_off;
-                T ea[V], eb[V];
-                if (direct) {
-                    *reinterpret_cast<uint4*>(ea) = *reinterpret_cast<const uint4*>(xa + o);
-                } else {
+                T ea[V];
 #pragma unroll
-                    for (int k = 0; k < V; ++k)
-                        ea[k] = rv ? xp[xr * g.W + pmod(col0 + k, g.W)] : T(0.0f);
-                    *reinterpret_cast<uint4*>(xa + o) = *reinterpret_cast<const uint4*>(ea);
-                }
-#pragma unroll
-                for (int k = 0; k < V; ++k) {
-                    const int64_t cc = col0 + k;
-                    const bool in = own && cc >= 0 && cc < g.W;
-                    // inside the image the own pixel equals the forward one
-                    eb[k] = in ? (direct ? ea[k] : xp[orow * g.W + cc]) : T(0.0f);
-                }
-                *reinterpret_cast<uint4*>(xb + o) = *reinterpret_cast<const uint4*>(eb);
+                for (int k = 0; k < V; ++k)
+                    ea[k] = rv ? xp[xr * g.W + pmod(col0 + k, g.W)] : T(0.0f);
+                *reinterpret_cast<uint4*>(xa + (c * XH + i) * XW + jv * V) =
+                    *reinterpret_cast<const uint4*>(ea);
             }
             named_sync(1, NCONS);
         }
         // prefetch the next tile's x while this one computes
         if (tile + gridDim.x < g.ntiles) issue_x(tile + gridDim.x, xa0 + (buf ^ 1) * xtile);
-        const T* xmsrc = border ? xb : xa;
 
         float u[NC][V], z[V];
 #pragma unroll
@@ -406,18 +416,35 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
 #pragma unroll
             for (int c = 0; c < NC; ++c) u[c][i] = 0.f;
         }
+        const int64_t gcol0 = static_cast<int64_t>(w0) - XC + tc * V;  // image column of window element 0
 
         for (int dx = -Rx; dx <= Rx; ++dx) {
             if (!tab.row_any[dx + MAXR]) continue;
-            uint32_t xf[NC][LF / EPW], xm[NC][LM / EPW];
+            uint32_t xf[NC][FWH - FWL], xm[NC][MWH - MWL];
 #pragma unroll
             for (int c = 0; c < NC; ++c)
-                lds_words(xf[c], xa + (c * XH + tr + dx + Rx) * XW + tc * V + XC + FB);
-            const bool rinv = tab.row_inv[dx + MAXR];
-            if (rinv) {
+                load_win<FWL, FWH, FWL>(xf[c], reinterpret_cast<const uint32_t*>(
+                    xa + (c * XH + tr + dx + Rx) * XW + tc * V));
+            if (tab.row_inv[dx + MAXR]) {
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
-                    lds_words(xm[c], xmsrc + (c * XH + tr - dx + Rx) * XW + tc * V + XC + MB);
+                    load_win<MWL, MWH, MWL>(xm[c], reinterpret_cast<const uint32_t*>(
+                        xa + (c * XH + tr - dx + Rx) * XW + tc * V));
+                // the mirror term reads x only inside the image
+                if (row_border || col_border) {
+                    const int64_t grow = static_cast<int64_t>(h0) + tr - dx;
+                    const bool rin = grow >= 0 && grow < g.H;
+#pragma unroll
+                    for (int k = 0; k < (MWH - MWL) * EPW; ++k) {
+                        const int64_t gc = gcol0 + MWL * EPW + k;
+                        if (!rin || gc < 0 || gc >= g.W) {
+                            const uint32_t keep =
+                                EPW == 1 ? 0u : ((k & 1) ? 0x0000FFFFu : 0xFFFF0000u);
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) xm[c][k / EPW] &= keep;
+                        }
+                    }
+                }
             }
             const int mrow0 = tr + (dx > 0 ? dx : 0);
             static_for<0, NDY>([&](auto jc) {
@@ -438,12 +465,13 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 if constexpr (NSC_FAST_EXPERIMENT == 1) {
                     z[0] += __uint_as_float(wv[0] ^ wv[1] ^ wv[2] ^ wv[3]);
                 } else {
-                static_for<0, V>([&](auto ic) {
-                    constexpr int i = decltype(ic)::value;
+                    static_for<0, V>([&](auto ic) {
+                        constexpr int i = decltype(ic)::value;
 #pragma unroll
-                    for (int c = 0; c < NC; ++c) fma_e<T, i, dy - FB + i>(u[c][i], wv, xf[c]);
-                    add_e<T, i>(z[i], wv);
-                });
+                        for (int c = 0; c < NC; ++c)
+                            fma_e<T, i, XC + dy + i - FWL * EPW>(u[c][i], wv, xf[c]);
+                        add_e<T, i>(z[i], wv);
+                    });
                 }
                 if (NSC_FAST_EXPERIMENT != 1 && (e & kInvBit)) {
                     constexpr int moff = mo - dy;               // >= 0
@@ -459,7 +487,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         constexpr int i = decltype(ic)::value;
 #pragma unroll
                         for (int c = 0; c < NC; ++c)
-                            fma_e<T, kk + i, -dy - MB + i>(u[c][i], mw, xm[c]);
+                            fma_e<T, kk + i, XC - dy + i - MWL * EPW>(u[c][i], mw, xm[c]);
                         add_e<T, kk + i>(z[i], mw);
                     });
                 }
@@ -470,6 +498,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 }
             });
         }
+
         // ---- store
         const int64_t h = h0 + tr;
         const int64_t wcol = w0 + tc * V;

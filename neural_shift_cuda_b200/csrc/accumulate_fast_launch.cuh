@@ -2,10 +2,13 @@
 // by the per-dtype instantiation files so the kernels compile in parallel.
 #pragma once
 
+#include <cstdio>
+
 #include "accumulate_fast.cuh"
 
 namespace nsc {
 int fast_sm_count();
+void fast_set_decline(const char* why);
 
 namespace fast {
 
@@ -13,20 +16,35 @@ template <typename T, int NC, int DYMIN, int DYMAX>
 bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
             cudaStream_t stream) {
-    // ring depth: as many weight stages (<= 12) as fit next to the three
+    // ring depth: as many weight stages (<= 12) as fit next to the two
     // x tiles in the 227 KB a CTA may use
-    const size_t fixed = 3ull * NC * g.XH * g.XW * sizeof(T) + 16 + 16 + 128;
+    const size_t fixed = 2ull * NC * g.XH * g.XW * sizeof(T) + 16 + 16 + 128;
     const size_t per_stage = g.stage_stride + 2 * sizeof(uint64_t);
     const size_t cap = 227u * 1024u;
-    if (fixed + 3 * per_stage > cap) return false;
+    if (fixed + 3 * per_stage > cap) {
+        fast_set_decline("shared memory");
+        return false;
+    }
     size_t ns = (cap - fixed) / per_stage;
     if (ns > 12) ns = 12;
     g.nstage = static_cast<int32_t>(ns);
     const size_t smem = fixed + ns * per_stage;
     auto k = acc_fast_kernel<T, NC, DYMIN, DYMAX>;
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, k) != cudaSuccess ||
+        attr.maxThreadsPerBlock < NTHREADS) {
+        cudaGetLastError();
+        static thread_local char why[160];
+        snprintf(why, sizeof(why),
+                 "CTA of %d threads exceeds the kernel's limit of %d (%d registers)",
+                 NTHREADS, attr.maxThreadsPerBlock, attr.numRegs);
+        fast_set_decline(why);
+        return false;
+    }
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess) {
         cudaGetLastError();
+        fast_set_decline("dynamic shared memory attribute");
         return false;
     }
     const int64_t nsm = fast_sm_count();
@@ -40,18 +58,12 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
 }  // namespace fast
 }  // namespace nsc
 
+#define NSC_FAST_ONE(T, NC, A, B)                                                  \
+    template bool nsc::fast::launch<T, NC, A, B>(const CUtensorMap&,                 \
+        const CUtensorMap&, const void*, void*, void*, const FastTable&, Geo,        \
+        unsigned int*, cudaStream_t);
 #define NSC_FAST_INSTANTIATE(T, NC)                                                  \
-    template bool nsc::fast::launch<T, NC, 0, 4>(const CUtensorMap&, const CUtensorMap&, const void*,    \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
-    template bool nsc::fast::launch<T, NC, 0, 8>(const CUtensorMap&, const CUtensorMap&, const void*,    \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
-    template bool nsc::fast::launch<T, NC, 0, 12>(const CUtensorMap&, const CUtensorMap&, const void*,   \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
-    template bool nsc::fast::launch<T, NC, 0, 16>(const CUtensorMap&, const CUtensorMap&, const void*,   \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
-    template bool nsc::fast::launch<T, NC, -4, 4>(const CUtensorMap&, const CUtensorMap&, const void*,   \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
-    template bool nsc::fast::launch<T, NC, -8, 8>(const CUtensorMap&, const CUtensorMap&, const void*,   \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);          \
-    template bool nsc::fast::launch<T, NC, -12, 12>(const CUtensorMap&, const CUtensorMap&, const void*, \
-        void*, void*, const FastTable&, Geo, unsigned int*, cudaStream_t);
+    NSC_FAST_ONE(T, NC, 0, 2) NSC_FAST_ONE(T, NC, 0, 4) NSC_FAST_ONE(T, NC, 0, 6)   \
+    NSC_FAST_ONE(T, NC, 0, 8) NSC_FAST_ONE(T, NC, 0, 10) NSC_FAST_ONE(T, NC, 0, 12) \
+    NSC_FAST_ONE(T, NC, 0, 16) NSC_FAST_ONE(T, NC, -4, 4) NSC_FAST_ONE(T, NC, -8, 8) \
+    NSC_FAST_ONE(T, NC, -12, 12)

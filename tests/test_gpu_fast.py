@@ -53,7 +53,11 @@ def test_fast_matches_oracle_and_generic(cuda, case):
     g = torch.Generator().manual_seed(1)
     x = torch.rand(B, C, H, W, generator=g).to(dt)
     w = _w(len(rows), B, Cw, H, W, sh, dt, 2)
-    U, Z = nsc.accumulate_uz(x.to(cuda), w.to(cuda), sh)
+    os.environ["NSC_REQUIRE_FAST"] = "1"   # fail if the tiled path declines
+    try:
+        U, Z = nsc.accumulate_uz(x.to(cuda), w.to(cuda), sh)
+    finally:
+        del os.environ["NSC_REQUIRE_FAST"]
     Ug, Zg = _generic(nsc.accumulate_uz, x.to(cuda), w.to(cuda), sh)
     Ur, Zr = O.accumulate_uz(x, w.expand(-1, C, -1, -1) if Cw == 1 else w, sh)
     torch.testing.assert_close(U.cpu(), Ur, rtol=1e-5, atol=1e-5)
