@@ -19,7 +19,7 @@
 namespace nsc {
 namespace fast {
 
-template <typename T, int NC, int DYMIN, int DYMAX>
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
 bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x,
             void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
@@ -47,25 +47,25 @@ int sm_count() {
 }
 
 template <typename T, int NC>
-bool by_bucket(bool half, int K, const CUtensorMap& map, const CUtensorMap& map2,
+bool by_bucket(bool exact, int K, const CUtensorMap& map, const CUtensorMap& map2,
                const void* x, void* U, void* Z, const fast::FastTable& tab,
                const fast::Geo& g, unsigned int* to, cudaStream_t st) {
-#define NSC_B(A, B) return fast::launch<T, NC, A, B>(map, map2, x, U, Z, tab, g, to, st)
-    if (half) {
+#define NSC_B(A, B, E) return fast::launch<T, NC, A, B, E>(map, map2, x, U, Z, tab, g, to, st)
+    if (exact) {
         switch (K) {
-            case 2: NSC_B(0, 2);
-            case 4: NSC_B(0, 4);
-            case 6: NSC_B(0, 6);
-            case 8: NSC_B(0, 8);
-            case 10: NSC_B(0, 10);
-            case 12: NSC_B(0, 12);
-            default: NSC_B(0, 16);
+            case 2: NSC_B(0, 2, true);
+            case 4: NSC_B(0, 4, true);
+            case 6: NSC_B(0, 6, true);
+            case 8: NSC_B(0, 8, true);
+            case 10: NSC_B(0, 10, true);
+            case 12: NSC_B(0, 12, true);
+            default: NSC_B(0, 16, true);
         }
     }
     switch (K) {
-        case 4: NSC_B(-4, 4);
-        case 8: NSC_B(-8, 8);
-        default: NSC_B(-12, 12);
+        case 4: NSC_B(-4, 4, false);
+        case 8: NSC_B(-8, 8, false);
+        default: NSC_B(-12, 12, false);
     }
 #undef NSC_B
 }
@@ -130,13 +130,41 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
             prev_dy = dy;
         }
     }
-    const bool half = dymin >= 0;
-    const int span = half ? dymax : (dymax > -dymin ? dymax : -dymin);
+    for (int dx = -MAXR; dx <= MAXR; ++dx)
+        for (int dy = -MAXR; dy <= MAXR; ++dy) {
+            const int e = tab.s[dx + MAXR][dy + MAXR];
+            if (e < 0) continue;
+            const uint64_t bit = 1ull << (dy + MAXR);
+            tab.present[dx + MAXR] |= bit;
+            if (e & kInvBit) tab.inv[dx + MAXR] |= bit;
+            if (e & kPairFirst) tab.first[dx + MAXR] |= bit;
+            if (e & kPairSecond) tab.second[dx + MAXR] |= bit;
+        }
+    // Canonical half-plane table of radius R: compile-time entry pattern.
+    bool exact = dymin >= 0 && dymax == rx && rx >= 1;
+    for (int dx = -rx; exact && dx <= rx; ++dx)
+        for (int dy = 0; dy <= rx; ++dy) {
+            const int e = tab.s[dx + MAXR][dy + MAXR];
+            bool want = dy > 0 || dx >= 0;
+            if ((e >= 0) != want) { exact = false; break; }
+            if (e < 0) continue;
+            const bool inv = e & kInvBit;
+            const bool first = e & kPairFirst, second = e & kPairSecond;
+            const bool want_inv = dy > 0 || dx != 0;
+            const bool want_first = dy > 0 && (dy & 1) && dy < rx;
+            const bool want_second = dy > 0 && !(dy & 1);
+            if (inv != want_inv || first != want_first || second != want_second) {
+                exact = false;
+                break;
+            }
+        }
+    tab.Rdy = dymax;
     int K;
-    if (half) {
-        K = span <= 12 ? (span + 1) / 2 * 2 : 16;
-        if (K < 2) K = 2;
+    if (exact) {
+        K = rx <= 12 ? (rx + 1) / 2 * 2 : 16;
+        if (rx > 16) DECLINE("radius");
     } else {
+        const int span = dymax > -dymin ? dymax : -dymin;
         K = span <= 4 ? 4 : span <= 8 ? 8 : span <= 12 ? 12 : 16;
         if (K > 12) DECLINE("dy range");
     }
@@ -172,13 +200,13 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     if (!to) DECLINE("timeout counter");
     (void)sm_count;
     if (xd == NSC_F16)
-        return NC == 1 ? by_bucket<__half, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
-                       : by_bucket<__half, 3>(half, K, map, map2, x, U, Z, tab, g, to, stream);
+        return NC == 1 ? by_bucket<__half, 1>(exact, K, map, map2, x, U, Z, tab, g, to, stream)
+                       : by_bucket<__half, 3>(exact, K, map, map2, x, U, Z, tab, g, to, stream);
     if (xd == NSC_BF16)
-        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
-                       : by_bucket<__nv_bfloat16, 3>(half, K, map, map2, x, U, Z, tab, g, to, stream);
-    return NC == 1 ? by_bucket<float, 1>(half, K, map, map2, x, U, Z, tab, g, to, stream)
-                   : by_bucket<float, 3>(half, K, map, map2, x, U, Z, tab, g, to, stream);
+        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(exact, K, map, map2, x, U, Z, tab, g, to, stream)
+                       : by_bucket<__nv_bfloat16, 3>(exact, K, map, map2, x, U, Z, tab, g, to, stream);
+    return NC == 1 ? by_bucket<float, 1>(exact, K, map, map2, x, U, Z, tab, g, to, stream)
+                   : by_bucket<float, 3>(exact, K, map, map2, x, U, Z, tab, g, to, stream);
 }
 
 int fast_sm_count() { return sm_count(); }

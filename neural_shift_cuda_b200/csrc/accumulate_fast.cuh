@@ -36,7 +36,7 @@
 
 // Build-time switch for throughput experiments (0 in every shipped build):
 // 1 = stream the weights without the arithmetic, 2 = arithmetic without
-// waiting for the weights.
+// waiting for the weights, 3 = as 1 and without staging x.
 #ifndef NSC_FAST_EXPERIMENT
 #define NSC_FAST_EXPERIMENT 0
 #endif
@@ -62,10 +62,15 @@ constexpr int kPairSecond = 0x2000;  // second plane of the previous entry's cop
 constexpr int kSMask = 0x7FF;
 
 struct FastTable {
-    int16_t s[2 * MAXR + 1][2 * MAXR + 1];  // [dx+MAXR][dy+MAXR] -> s | inv, or -1
+    int16_t s[2 * MAXR + 1][2 * MAXR + 1];  // [dx+MAXR][dy+MAXR] -> s | flags, or -1
+    // per dx row, bit (dy + MAXR): entry present / has a mirror term /
+    // first of a paired copy / second of a paired copy
+    uint64_t present[2 * MAXR + 1], inv[2 * MAXR + 1];
+    uint64_t first[2 * MAXR + 1], second[2 * MAXR + 1];
     uint8_t row_any[2 * MAXR + 1];
     uint8_t row_inv[2 * MAXR + 1];
     int32_t Rx;                             // max |dx|
+    int32_t Rdy;                            // max dy (canonical half-plane tables)
 };
 
 struct Geo {
@@ -215,6 +220,53 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
+// 16 / 8 / 4-byte shared-memory loads by 32-bit shared address.  volatile
+// keeps them ordered after the mbarrier waits (also volatile asm).
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+template <int N>
+__device__ __forceinline__ void lds_words32(uint32_t* dst, uint32_t a) {
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k) {
+        const uint4 v = lds128(a + 16 * k);
+        dst[4 * k] = v.x; dst[4 * k + 1] = v.y; dst[4 * k + 2] = v.z; dst[4 * k + 3] = v.w;
+    }
+}
+// Load words [K, HI) of the shared-memory row at byte address `a` into
+// d[K - LO ...] with the widest aligned vector (the row base is 16-byte
+// aligned).
+template <int K, int HI, int LO, int N>
+__device__ __forceinline__ void load_win32(uint32_t (&d)[N], uint32_t a) {
+    if constexpr (K < HI) {
+        if constexpr (K % 4 == 0 && K + 4 <= HI) {
+            const uint4 v = lds128(a + 4 * K);
+            d[K - LO] = v.x; d[K - LO + 1] = v.y; d[K - LO + 2] = v.z; d[K - LO + 3] = v.w;
+            load_win32<K + 4, HI, LO>(d, a);
+        } else if constexpr (K % 2 == 0 && K + 2 <= HI) {
+            const uint2 v = lds64(a + 4 * K);
+            d[K - LO] = v.x; d[K - LO + 1] = v.y;
+            load_win32<K + 2, HI, LO>(d, a);
+        } else {
+            d[K - LO] = lds32(a + 4 * K);
+            load_win32<K + 1, HI, LO>(d, a);
+        }
+    }
+}
+
 // Load words [K, HI) of a shared-memory row into d[K - LO ...], using the
 // widest aligned vector (the row base is 16-byte aligned).
 template <int K, int HI, int LO, int N>
@@ -235,7 +287,12 @@ __device__ __forceinline__ void load_win(uint32_t (&d)[N], const uint32_t* p) {
     }
 }
 
-template <typename T, int NC, int DYMIN, int DYMAX>
+// EXACT: the table is the canonical half-plane table of radius Rdy <= DYMAX
+// (for every dx: dy = 1..Rdy with mirror terms, plus (dx, 0) for dx >= 0
+// with a mirror term for dx != 0; weight planes consecutive along dy), so
+// which entries exist, which have a mirror term and how they pair into
+// copies are compile-time facts of dy and need no per-shift table tests.
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
 __global__ void __launch_bounds__(NTHREADS, 1)
 acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 const __grid_constant__ CUtensorMap wmap2, const T* __restrict__ x,
@@ -374,7 +431,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
     };
 
     int buf = 0;
-    if (blockIdx.x < g.ntiles) issue_x(blockIdx.x, xa0);
+    if (NSC_FAST_EXPERIMENT != 3 && blockIdx.x < g.ntiles) issue_x(blockIdx.x, xa0);
     for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
         const TileId id = decode_tile(tile, g, TW, cgroups);
         const int64_t b = id.b;
@@ -389,7 +446,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         cp_async_wait_all();
         named_sync(1, NCONS);
         if (*(volatile int*)&abort_flag) break;
-        if (row_border || col_border) {
+        if (NSC_FAST_EXPERIMENT != 3 && (row_border || col_border)) {
             for (int idx = tid; idx < xtotal; idx += NCONS) {
                 int c, i, jv;
                 int64_t r, col0, xr;
@@ -407,7 +464,8 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             named_sync(1, NCONS);
         }
         // prefetch the next tile's x while this one computes
-        if (tile + gridDim.x < g.ntiles) issue_x(tile + gridDim.x, xa0 + (buf ^ 1) * xtile);
+        if (NSC_FAST_EXPERIMENT != 3 && tile + gridDim.x < g.ntiles)
+            issue_x(tile + gridDim.x, xa0 + (buf ^ 1) * xtile);
 
         float u[NC][V], z[V];
 #pragma unroll
@@ -421,15 +479,17 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         for (int dx = -Rx; dx <= Rx; ++dx) {
             if (!tab.row_any[dx + MAXR]) continue;
             uint32_t xf[NC][FWH - FWL], xm[NC][MWH - MWL];
+            const uint32_t xa32 = smem_u32(xa) + static_cast<uint32_t>(tc * V * sizeof(T));
+            const uint32_t xrow = static_cast<uint32_t>(XH * XW * sizeof(T));
 #pragma unroll
             for (int c = 0; c < NC; ++c)
-                load_win<FWL, FWH, FWL>(xf[c], reinterpret_cast<const uint32_t*>(
-                    xa + (c * XH + tr + dx + Rx) * XW + tc * V));
+                load_win32<FWL, FWH, FWL>(xf[c], xa32 + c * xrow +
+                    static_cast<uint32_t>((tr + dx + Rx) * XW * sizeof(T)));
             if (tab.row_inv[dx + MAXR]) {
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
-                    load_win<MWL, MWH, MWL>(xm[c], reinterpret_cast<const uint32_t*>(
-                        xa + (c * XH + tr - dx + Rx) * XW + tc * V));
+                    load_win32<MWL, MWH, MWL>(xm[c], xa32 + c * xrow +
+                        static_cast<uint32_t>((tr - dx + Rx) * XW * sizeof(T)));
                 // the mirror term reads x only inside the image
                 if (row_border || col_border) {
                     const int64_t grow = static_cast<int64_t>(h0) + tr - dx;
@@ -446,23 +506,29 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                     }
                 }
             }
+            // Shared-memory byte offsets of this thread's main and mirror
+            // weight rows inside a stage, hoisted out of the shift loop.
             const int mrow0 = tr + (dx > 0 ? dx : 0);
-            static_for<0, NDY>([&](auto jc) {
-                constexpr int dy = DYMIN + decltype(jc)::value;
-                const int e = tab.s[dx + MAXR][dy + MAXR];
-                if (e < 0) return;
-                const bool second = e & kPairSecond;
-                if (NSC_FAST_EXPERIMENT != 2 && !second && !dead &&
-                    !mbar_wait(&full[stage], phase, timeouts)) {
-                    dead = true;
-                    *(volatile int*)&abort_flag = 1;
+            const uint32_t off_main = static_cast<uint32_t>((mrow0 * BW + tc * V) * sizeof(T));
+            const uint32_t off_mir = static_cast<uint32_t>(((mrow0 - dx) * BW + tc * V) * sizeof(T));
+            const uint64_t m_pres = tab.present[dx + MAXR], m_inv = tab.inv[dx + MAXR];
+            const uint64_t m_first = tab.first[dx + MAXR], m_second = tab.second[dx + MAXR];
+            const uint32_t stages32 = smem_u32(stages);
+            uint32_t stp = stages32 + stage * g.stage_stride;
+            auto one = [&](auto dyc, const bool second, const bool first, const bool inv) {
+                constexpr int dy = decltype(dyc)::value;
+                if (NSC_FAST_EXPERIMENT != 2 && !second && !dead) {
+                    if (!mbar_try_wait(&full[stage], phase) &&
+                        !mbar_wait(&full[stage], phase, timeouts)) {
+                        dead = true;
+                        *(volatile int*)&abort_flag = 1;
+                    }
                 }
-                const T* st = reinterpret_cast<const T*>(
-                    stages + stage * g.stage_stride + (second ? g.plane_bytes : 0u));
+                const uint32_t sp = stp + (second ? g.plane_bytes : 0u);
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
-                lds_words(wv, st + mrow0 * BW + tc * V + mo);
-                if constexpr (NSC_FAST_EXPERIMENT == 1) {
+                lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
+                if constexpr (NSC_FAST_EXPERIMENT == 1 || NSC_FAST_EXPERIMENT == 3) {
                     z[0] += __uint_as_float(wv[0] ^ wv[1] ^ wv[2] ^ wv[3]);
                 } else {
                     static_for<0, V>([&](auto ic) {
@@ -473,16 +539,14 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         add_e<T, i>(z[i], wv);
                     });
                 }
-                if (NSC_FAST_EXPERIMENT != 1 && (e & kInvBit)) {
+                if (NSC_FAST_EXPERIMENT != 1 && NSC_FAST_EXPERIMENT != 3 && inv) {
                     constexpr int moff = mo - dy;               // >= 0
                     constexpr int kk = moff % V;
                     constexpr int mb = moff - kk;
                     uint32_t mw[2 * V / EPW];
-                    lds_words<V / EPW>(*reinterpret_cast<uint32_t(*)[V / EPW]>(mw),
-                                       st + (mrow0 - dx) * BW + tc * V + mb);
+                    lds_words32<V / EPW>(mw, sp + off_mir + mb * sizeof(T));
                     if constexpr (kk != 0)
-                        lds_words<V / EPW>(*reinterpret_cast<uint32_t(*)[V / EPW]>(mw + V / EPW),
-                                           st + (mrow0 - dx) * BW + tc * V + mb + V);
+                        lds_words32<V / EPW>(mw + V / EPW, sp + off_mir + (mb + V) * sizeof(T));
                     static_for<0, V>([&](auto ic) {
                         constexpr int i = decltype(ic)::value;
 #pragma unroll
@@ -491,12 +555,36 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         add_e<T, kk + i>(z[i], mw);
                     });
                 }
-                if (!(e & kPairFirst)) {   // copy fully used: release it
+                if (!first) {   // copy fully used: release it
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[stage]);
                     if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+                    stp = stages32 + stage * g.stage_stride;
                 }
-            });
+            };
+            if constexpr (EXACT) {
+                // (dx, 0): a single copy, mirror term unless dx == 0
+                if (dx >= 0) one(std::integral_constant<int, 0>{}, false, false, dx != 0);
+                const int R = tab.Rdy;
+                // dy = 1..R: (odd, even) pairs share a copy; a trailing odd
+                // dy (R odd) is single.
+                static_for<1, DYMAX + 1>([&](auto jc) {
+                    constexpr int dy = decltype(jc)::value;
+                    if (dy > R) return;
+                    if constexpr (dy & 1)
+                        one(jc, false, dy < R, true);
+                    else
+                        one(jc, true, false, true);
+                });
+            } else {
+                static_for<0, NDY>([&](auto jc) {
+                    constexpr int dy = DYMIN + decltype(jc)::value;
+                    constexpr int bit = dy + MAXR;
+                    if (!((m_pres >> bit) & 1u)) return;
+                    one(std::integral_constant<int, dy>{}, (m_second >> bit) & 1u,
+                        (m_first >> bit) & 1u, (m_inv >> bit) & 1u);
+                });
+            }
         }
 
         // ---- store

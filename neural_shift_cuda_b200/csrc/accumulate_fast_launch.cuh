@@ -12,7 +12,7 @@ void fast_set_decline(const char* why);
 
 namespace fast {
 
-template <typename T, int NC, int DYMIN, int DYMAX>
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
 bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
             cudaStream_t stream) {
@@ -29,7 +29,7 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
     if (ns > 12) ns = 12;
     g.nstage = static_cast<int32_t>(ns);
     const size_t smem = fixed + ns * per_stage;
-    auto k = acc_fast_kernel<T, NC, DYMIN, DYMAX>;
+    auto k = acc_fast_kernel<T, NC, DYMIN, DYMAX, EXACT>;
     cudaFuncAttributes attr;
     if (cudaFuncGetAttributes(&attr, k) != cudaSuccess ||
         attr.maxThreadsPerBlock < NTHREADS) {
@@ -58,12 +58,13 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
 }  // namespace fast
 }  // namespace nsc
 
-#define NSC_FAST_ONE(T, NC, A, B)                                                  \
-    template bool nsc::fast::launch<T, NC, A, B>(const CUtensorMap&,                 \
+#define NSC_FAST_ONE(T, NC, A, B, E)                                               \
+    template bool nsc::fast::launch<T, NC, A, B, E>(const CUtensorMap&,              \
         const CUtensorMap&, const void*, void*, void*, const FastTable&, Geo,        \
         unsigned int*, cudaStream_t);
 #define NSC_FAST_INSTANTIATE(T, NC)                                                  \
-    NSC_FAST_ONE(T, NC, 0, 2) NSC_FAST_ONE(T, NC, 0, 4) NSC_FAST_ONE(T, NC, 0, 6)   \
-    NSC_FAST_ONE(T, NC, 0, 8) NSC_FAST_ONE(T, NC, 0, 10) NSC_FAST_ONE(T, NC, 0, 12) \
-    NSC_FAST_ONE(T, NC, 0, 16) NSC_FAST_ONE(T, NC, -4, 4) NSC_FAST_ONE(T, NC, -8, 8) \
-    NSC_FAST_ONE(T, NC, -12, 12)
+    NSC_FAST_ONE(T, NC, 0, 2, true) NSC_FAST_ONE(T, NC, 0, 4, true)                  \
+    NSC_FAST_ONE(T, NC, 0, 6, true) NSC_FAST_ONE(T, NC, 0, 8, true)                  \
+    NSC_FAST_ONE(T, NC, 0, 10, true) NSC_FAST_ONE(T, NC, 0, 12, true)                \
+    NSC_FAST_ONE(T, NC, 0, 16, true) NSC_FAST_ONE(T, NC, -4, 4, false)               \
+    NSC_FAST_ONE(T, NC, -8, 8, false) NSC_FAST_ONE(T, NC, -12, 12, false)
