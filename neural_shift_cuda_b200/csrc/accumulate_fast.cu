@@ -211,6 +211,41 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
 
 int fast_sm_count() { return sm_count(); }
 
+namespace {
+// Tile-ticket counters of the tiled kernels: 64 slots per device, handed
+// out round-robin and zeroed in-stream before each launch.  A slot is reused
+// only 64 launches later, so launches on concurrent streams do not share a
+// counter unless more than 64 of them are in flight at once.
+constexpr int kTicketSlots = 64;
+static __device__ unsigned long long g_tickets[kTicketSlots];
+std::mutex g_ticket_mu;
+unsigned long long* g_ticket_base[64] = {};
+unsigned g_ticket_next[64] = {};
+}  // namespace
+
+unsigned long long* tile_ticket(cudaStream_t stream) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    unsigned long long* p;
+    {
+        std::lock_guard<std::mutex> lock(g_ticket_mu);
+        if (!g_ticket_base[dev]) {
+            void* a = nullptr;
+            if (cudaGetSymbolAddress(&a, g_tickets) != cudaSuccess) {
+                cudaGetLastError();
+                return nullptr;
+            }
+            g_ticket_base[dev] = static_cast<unsigned long long*>(a);
+        }
+        p = g_ticket_base[dev] + (g_ticket_next[dev]++ % kTicketSlots);
+    }
+    if (cudaMemsetAsync(p, 0, sizeof(*p), stream) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return p;
+}
+
 const char* fast_decline_reason() { return g_decline; }
 void fast_set_decline(const char* why) { g_decline = why; }
 

@@ -297,7 +297,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 const __grid_constant__ CUtensorMap wmap2, const T* __restrict__ x,
                 float* __restrict__ U, float* __restrict__ Zo, const FastTable tab,
-                const Geo g, unsigned int* timeouts) {
+                const Geo g, unsigned int* timeouts,
+                unsigned long long* __restrict__ ticket) {
     constexpr int V = 16 / static_cast<int>(sizeof(T));
     constexpr int EPW = 4 / static_cast<int>(sizeof(T));   // elements per word
     constexpr int TW = TPR * V;
@@ -322,7 +323,14 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
     uint64_t* full = reinterpret_cast<uint64_t*>(
         (reinterpret_cast<uintptr_t>(xa0 + 2 * xtile) + 15) & ~uintptr_t(15));
     uint64_t* empty = full + NSTAGE;
-    int& abort_flag = *reinterpret_cast<int*>(empty + NSTAGE);
+    // Dynamic tile order: the producer draws tickets from a global counter
+    // (two tiles ahead) and publishes them in a 4-slot ring.  Tiles are then
+    // processed in raster order across all CTAs, so vertically and
+    // horizontally adjacent tiles -- whose weight boxes overlap -- run at the
+    // same time and their shared rows are served by L2.
+    uint64_t* tile_full = empty + NSTAGE;
+    int64_t* tile_ring = reinterpret_cast<int64_t*>(tile_full + 4);
+    int& abort_flag = *reinterpret_cast<int*>(tile_ring + 4);
 
     const int tid = threadIdx.x;
     if (tid == 0) {
@@ -330,6 +338,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], NCONS / 32);
         }
+        for (int i = 0; i < 4; ++i) mbar_init(&tile_full[i], 1);
         abort_flag = 0;
         fence_mbar_init();
     }
@@ -345,7 +354,18 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         int stage = 0;
         uint32_t phase = 0;
         bool aborted = false;
-        for (int64_t tile = blockIdx.x; tile < g.ntiles && !aborted; tile += gridDim.x) {
+        auto fetch = [&](uint32_t k) {
+            const unsigned long long t = atomicAdd(ticket, 1ull);
+            *(volatile int64_t*)&tile_ring[k & 3] =
+                t < static_cast<unsigned long long>(g.ntiles) ? static_cast<int64_t>(t) : -1;
+            mbar_arrive(&tile_full[k & 3]);
+        };
+        fetch(0);
+        fetch(1);
+        for (uint32_t k = 0; !aborted; ++k) {
+            const int64_t tile = *(volatile int64_t*)&tile_ring[k & 3];
+            if (tile < 0) break;
+            fetch(k + 2);
             const TileId id = decode_tile(tile, g, TW, cgroups);
             const int64_t b = id.b;
             const int64_t wc = (g.Cw == 1) ? 0 : id.grp % cgroups;
@@ -430,9 +450,19 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         cp_async_commit();
     };
 
+    // Tile k of this CTA (ring slot k & 3), -1 when the schedule is done.
+    auto tile_at = [&](uint32_t k) -> int64_t {
+        if (!dead && !mbar_try_wait(&tile_full[k & 3], (k >> 2) & 1u) &&
+            !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts)) {
+            dead = true;
+            *(volatile int*)&abort_flag = 1;
+        }
+        return dead ? -1 : *(volatile int64_t*)&tile_ring[k & 3];
+    };
     int buf = 0;
-    if (NSC_FAST_EXPERIMENT != 3 && blockIdx.x < g.ntiles) issue_x(blockIdx.x, xa0);
-    for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+    int64_t tile = tile_at(0);
+    if (NSC_FAST_EXPERIMENT != 3 && tile >= 0) issue_x(tile, xa0);
+    for (uint32_t k = 0; tile >= 0; ++k) {
         const TileId id = decode_tile(tile, g, TW, cgroups);
         const int64_t b = id.b;
         const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
@@ -464,8 +494,8 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             named_sync(1, NCONS);
         }
         // prefetch the next tile's x while this one computes
-        if (NSC_FAST_EXPERIMENT != 3 && tile + gridDim.x < g.ntiles)
-            issue_x(tile + gridDim.x, xa0 + (buf ^ 1) * xtile);
+        const int64_t next = tile_at(k + 1);
+        if (NSC_FAST_EXPERIMENT != 3 && next >= 0) issue_x(next, xa0 + (buf ^ 1) * xtile);
 
         float u[NC][V], z[V];
 #pragma unroll
@@ -604,6 +634,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             }
         }
         buf ^= 1;
+        tile = next;
     }
     cp_async_wait_all();
 }

@@ -8,6 +8,8 @@
 
 namespace nsc {
 int fast_sm_count();
+// A zeroed tile-ticket counter for one launch on `stream` (nullptr on error).
+unsigned long long* tile_ticket(cudaStream_t stream);
 void fast_set_decline(const char* why);
 
 namespace fast {
@@ -16,9 +18,14 @@ template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
 bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
             cudaStream_t stream) {
+    unsigned long long* ticket = tile_ticket(stream);
+    if (!ticket) {
+        fast_set_decline("tile counter");
+        return false;
+    }
     // ring depth: as many weight stages (<= 12) as fit next to the two
     // x tiles in the 227 KB a CTA may use
-    const size_t fixed = 2ull * NC * g.XH * g.XW * sizeof(T) + 16 + 16 + 128;
+    const size_t fixed = 2ull * NC * g.XH * g.XW * sizeof(T) + 16 + 4 * 16 + 16 + 128;
     const size_t per_stage = g.stage_stride + 2 * sizeof(uint64_t);
     const size_t cap = 227u * 1024u;
     if (fixed + 3 * per_stage > cap) {
@@ -51,7 +58,7 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
     const unsigned grid = static_cast<unsigned>(g.ntiles < nsm ? g.ntiles : nsm);
     k<<<grid, NTHREADS, smem, stream>>>(map1, map2, static_cast<const T*>(x),
                                         static_cast<float*>(U),
-                                        static_cast<float*>(Z), tab, g, timeouts);
+                                        static_cast<float*>(Z), tab, g, timeouts, ticket);
     return true;
 }
 
