@@ -36,7 +36,8 @@
 
 // Build-time switch for throughput experiments (0 in every shipped build):
 // 1 = stream the weights without the arithmetic, 2 = arithmetic without
-// waiting for the weights, 3 = as 1 and without staging x.
+// waiting for the weights, 3 = as 1 and without staging x, 4 = arithmetic
+// only: no weight copies, no waits.
 #ifndef NSC_FAST_EXPERIMENT
 #define NSC_FAST_EXPERIMENT 0
 #endif
@@ -149,7 +150,11 @@ __device__ __forceinline__ void fma_e(float& acc, const uint32_t* w, const uint3
         acc = fmaf(__uint_as_float(w[WI]), __uint_as_float(x[XI]), acc);
     } else {
         const uint32_t ww = w[WI >> 1], xx = x[XI >> 1];
+#if NSC_FAST_EXPERIMENT == 5
+        constexpr int sel = 0;   // throughput probe only: wrong results
+#else
         constexpr int sel = ((WI & 1) << 1) | (XI & 1);
+#endif
         if constexpr (Elem<T>::kind == 0) {
             if constexpr (sel == 0)
                 asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.f16 %0, a0, b0, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
@@ -238,11 +243,27 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
     return v;
 }
+// Non-volatile 16-byte shared load: free to be scheduled early.  Callers
+// order it after the data became visible through a data dependency on the
+// address (see `after`).
+__device__ __forceinline__ uint4 lds128nv(uint32_t a) {
+    uint4 v;
+    asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+// Returns `a` through a volatile asm, so values computed from the result
+// cannot be computed before the preceding volatile asm (the mbarrier wait).
+__device__ __forceinline__ uint32_t after(uint32_t a) {
+    uint32_t r;
+    asm volatile("mov.b32 %0, %1;" : "=r"(r) : "r"(a));
+    return r;
+}
 template <int N>
 __device__ __forceinline__ void lds_words32(uint32_t* dst, uint32_t a) {
 #pragma unroll
     for (int k = 0; k < N / 4; ++k) {
-        const uint4 v = lds128(a + 16 * k);
+        const uint4 v = lds128nv(a + 16 * k);
         dst[4 * k] = v.x; dst[4 * k + 1] = v.y; dst[4 * k + 2] = v.z; dst[4 * k + 3] = v.w;
     }
 }
@@ -383,6 +404,12 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         break;
                     }
                     const bool pair = e & kPairFirst;
+                    if (NSC_FAST_EXPERIMENT == 4) {   // handshake without a copy
+                        mbar_arrive(&full[stage]);
+                        ++it;
+                        if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+                        continue;
+                    }
                     mbar_arrive_expect_tx(&full[stage], pair ? 2 * g.plane_bytes
                                                              : g.plane_bytes);
                     const int mo = dy > 0 ? align_up(dy, V) : 0;
@@ -398,7 +425,8 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         }
         // Drain: the CTA must not exit with copies into its shared memory in
         // flight.  Wait (bounded) for the last NSTAGE loads to land.
-        const uint32_t n = it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE;
+        const uint32_t n = NSC_FAST_EXPERIMENT == 4 ? 0u
+                           : (it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE);
         for (uint32_t j = it - n; j < it; ++j)
             mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts);
         return;
@@ -554,7 +582,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         *(volatile int*)&abort_flag = 1;
                     }
                 }
-                const uint32_t sp = stp + (second ? g.plane_bytes : 0u);
+                const uint32_t sp = after(stp + (second ? g.plane_bytes : 0u));
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
                 lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
