@@ -1,0 +1,270 @@
+"""GPU tests of the model installers.
+
+* NECTR: the reference's own NECTR_models1 weights (tests/golden) through
+  the installed CUDA forward, against the reference's serial and patched
+  outputs (fp64).
+* GASD / NeKDe / NKD_mp: the model files are not part of the reference
+  checkout, so small stub models implement exactly the attributes the
+  installers call (`pre_activation`, `_collect_shifts`, the per-shift
+  weight producers, head mixing); the installed forwards are checked
+  against direct CPU restatements of the operators they implement (the
+  reference's own cached-path tests use the same approach,
+  tests/test_cached_forward_patches.py).
+"""
+
+import os
+from types import SimpleNamespace
+
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from neural_shift_cuda_b200 import integration as I
+from oracle import nsc_oracle as O
+from oracle.nectr_model import NECTR_denoiser
+
+pytestmark = pytest.mark.gpu
+
+GOLD_NECTR = torch.load(os.path.join(os.path.dirname(__file__), "golden",
+                                     "golden_nectr.pt"), weights_only=False)
+
+
+def _roll(x, dx, dy):
+    """gather convention: out(h, w) = x(h+dx, w+dy) circularly"""
+    return torch.roll(x, shifts=(-dx, -dy), dims=(-2, -1))
+
+
+# --------------------------------------------------------------- NECTR
+
+@pytest.mark.parametrize("act", sorted(GOLD_NECTR))
+def test_nectr_installed_forward_matches_reference(cuda, act):
+    c = GOLD_NECTR[act]
+    cls = type("NECTRPatched", (NECTR_denoiser,), {})
+    I.install_cuda_shift_nectr(cls)
+    m = cls(SimpleNamespace(**c["args"])).double()
+    m.load_state_dict(c["state"])
+    m = m.to(cuda)
+    x = c["x"].to(cuda)
+    with torch.no_grad():
+        U, Z = m(x)
+        U2, Z2, cache = m(x, store_cache=True)
+        U3, Z3 = m(x, cache=cache)
+        m.use_cuda_shift = False
+        Us, Zs = m(x)                  # the model's own serial forward
+    for u, z in ((U, Z), (U2, Z2), (U3, Z3)):
+        torch.testing.assert_close(u.cpu(), c["U_patched"], rtol=1e-9, atol=1e-10)
+        torch.testing.assert_close(u.cpu(), c["U_serial"], rtol=1e-9, atol=1e-10)
+        torch.testing.assert_close(z.cpu().to(c["Z_serial"].dtype), c["Z_serial"],
+                                   rtol=1e-9, atol=1e-10)
+    torch.testing.assert_close(Us.cpu(), c["U_serial"], rtol=1e-9, atol=1e-10)
+
+
+def test_nectr_fp32_and_bf16_inputs(cuda):
+    """Benchmark-shaped NECTR (latent 16, R = 5) at reduced size: fp32 vs
+    the serial forward, and bf16 weights/inputs with fp32 accumulation."""
+    torch.manual_seed(0)
+    args = SimpleNamespace(model_type="concat", residual_depth=2, proj_depth=1,
+                           latent_dim=16, patch_rad=1, output_activation="exp",
+                           window_rad=5, in_channel=1, blind=True)
+    cls = type("NECTRPatched2", (NECTR_denoiser,), {})
+    I.install_cuda_shift_nectr(cls)
+    m = cls(args).to(cuda)
+    g = torch.Generator().manual_seed(0)
+    x = (torch.rand(2, 1, 40, 48, generator=g)
+         + (25 / 255) * torch.randn(2, 1, 40, 48, generator=g)).to(cuda)
+    with torch.no_grad():
+        U, Z = m(x)
+        m.use_cuda_shift = False
+        Us, Zs = m(x)
+        m.use_cuda_shift = True
+        mb = m.bfloat16()
+        Ub, _ = mb(x.bfloat16())
+    torch.testing.assert_close(U, Us, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(Z.float(), Zs, rtol=1e-4, atol=1e-5)
+    assert Ub.dtype == torch.float32
+    assert (Ub - Us).abs().max() < 0.1   # bf16 weight head
+
+
+# ------------------------------------------------------------ stub models
+
+class _StubBase(nn.Module):
+    """The model contract the attention installers use."""
+
+    def __init__(self, C, R, heads, comp_box, table):
+        super().__init__()
+        self.window_rad = R
+        self.comp_box = comp_box
+        self.max_batch_shifts = None
+        self.output_activation = "softmax"
+        self.raw_head_mix = (nn.Parameter(torch.randn(C, heads))
+                             if heads not in (1, C) else None)
+        self.feat = nn.Conv2d(C, 4, 3, padding=1)
+        self.score = nn.Conv2d(8, heads, 1)
+        self._table = table
+        self._gather_core = True
+
+    def pre_activation(self, x, sigma=None):
+        return torch.tanh(self.feat(x))
+
+    def _collect_shifts(self):
+        return list(self._table)
+
+    def _weights(self, phi, shifts):
+        logits = torch.stack([self.score(torch.cat([phi, _roll(phi, s[0], s[1])], 1))
+                              for s in shifts], 0)
+        return list(F.softmax(logits, dim=0))          # (B, heads, H, W) each
+
+    def _all_shift_weights(self, phi, padded_phi, sig, shifts):
+        return self._weights(phi, shifts)
+
+    def _halfplane_weights(self, phi, padded_phi, sig, shifts):
+        return self._weights(phi, shifts)
+
+    def _head_mix_matrix(self):
+        return (F.softmax(self.raw_head_mix, dim=1)
+                if self.raw_head_mix is not None else None)
+
+    def _mix_heads(self, w, C, mat):
+        if w.shape[1] == 1:
+            return w.expand(-1, C, -1, -1)
+        if mat is not None:
+            return torch.einsum("ch,bhij->bcij", mat, w)
+        return w
+
+    def _normalise_sigma(self, x, sig):
+        return sig
+
+
+def _mixed(m, x):
+    C = x.shape[1]
+    phi = m.pre_activation(x)
+    w = torch.stack(m._weights(phi, m._collect_shifts()), 0)
+    mat = m._head_mix_matrix()
+    return torch.stack([m._mix_heads(w[i], C, mat) for i in range(w.shape[0])], 0)
+
+
+@pytest.mark.parametrize("comp_box", [True, False])
+@pytest.mark.parametrize("heads", [1, 2, 3])
+def test_gasd_installed_forward(cuda, comp_box, heads):
+    torch.manual_seed(1)
+    B, C, H, W, R = 2, 3, 12, 16, 2
+    table = [(dx, dy) for dx in range(-R, R + 1) for dy in range(-R, R + 1)]
+    cls = type("GASDStub", (_StubBase,), {"forward": lambda self, x, guide=None, sig=None, return_D=True: None})
+    I.install_cuda_shift_gasd(cls)
+    m = cls(C, R, heads, comp_box, table).double().to(cuda)
+    x = torch.rand(B, C, H, W, dtype=torch.float64, device=cuda)
+    with torch.no_grad():
+        D, Z = m(x)
+        w = _mixed(m, x).cpu()
+    sh = torch.tensor([(dx, dy, 0) for dx, dy in table])
+    if comp_box:
+        w = w * torch.stack([O.box_mask(H, W, dx, dy, w.dtype) for dx, dy in table])[:, None, None]
+    Dr, Lr = O.normalized_accumulate_uz(x.cpu(), w.reshape(-1, C, H, W), sh, False)
+    torch.testing.assert_close(D.cpu(), Dr, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(Z.cpu(), Lr.exp(), rtol=1e-10, atol=1e-10)
+    # K^T through the rolled weights and negated shifts
+    y = torch.rand_like(x)
+    with torch.no_grad():
+        KT = m._KT_action(y, guide=x)
+    ref = sum(torch.roll(w[i] * y.cpu(), shifts=(dx, dy), dims=(-2, -1))
+              for i, (dx, dy) in enumerate(table))
+    torch.testing.assert_close(KT.cpu(), ref, rtol=1e-10, atol=1e-10)
+
+
+def _symmetric_serial(x, w, rows, use_box):
+    """sum of forward and mirror terms of the symmetric operator"""
+    H, W = x.shape[-2:]
+    U = torch.zeros_like(x)
+    Z = torch.zeros_like(x)
+    for wf, (dx, dy, inv) in zip(w, rows):
+        if use_box:
+            wf = wf * O.box_mask(H, W, dx, dy, wf.dtype)
+        U = U + wf * _roll(x, dx, dy)
+        Z = Z + wf
+        if inv:
+            wi = torch.roll(wf, shifts=(dx, dy), dims=(-2, -1))
+            if use_box:
+                wi = wi * O.box_mask(H, W, -dx, -dy, wi.dtype)
+            U = U + wi * _roll(x, -dx, -dy)
+            Z = Z + wi
+    return U, Z
+
+
+@pytest.mark.parametrize("comp_box", [True, False])
+@pytest.mark.parametrize("heads", [1, 3])
+def test_nekde_installed_forward(cuda, comp_box, heads):
+    torch.manual_seed(2)
+    B, C, H, W, R = 2, 3, 11, 13, 2
+    rows = O.halfplane_shifts(R)
+    cls = type("NeKDeStub", (_StubBase,), {"forward": lambda self, x, guide=None, sig=None, return_D=True: None})
+    I.install_cuda_shift_attn(cls)
+    m = cls(C, R, heads, comp_box, rows).double().to(cuda)
+    x = torch.rand(B, C, H, W, dtype=torch.float64, device=cuda)
+    with torch.no_grad():
+        D, Z = m(x)
+        w = _mixed(m, x).cpu()
+        KT, Zk = m._KT_action(x, return_D=True)
+    U, Zr = _symmetric_serial(x.cpu(), w, rows, comp_box)
+    torch.testing.assert_close(D.cpu(), U / Zr, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(Z.cpu(), Zr, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(KT.cpu(), U, rtol=1e-10, atol=1e-10)
+
+
+@pytest.mark.parametrize("comp_box", [True, False])
+def test_metropolis_installed_forward(cuda, comp_box):
+    torch.manual_seed(3)
+    B, C, H, W, R = 2, 3, 10, 12, 2
+    rows = O.halfplane_shifts(R)
+    cls = type("MPStub", (_StubBase,), {"forward": lambda self, x, guide=None, sig=None, return_D=False: None})
+    I.install_cuda_shift_metropolis(cls)
+    m = cls(C, R, 1, comp_box, rows).double().to(cuda)
+    m.metropolis_eps = 1e-6
+    x = torch.rand(B, C, H, W, dtype=torch.float64, device=cuda)
+    with torch.no_grad():
+        Wx, dh = m(x, return_D=True)
+        w_half = _mixed(m, x).cpu().permute(1, 0, 2, 3, 4)
+    Wr, dr = O.metropolis_aggregate(w_half, x.cpu(), rows, comp_box, 1e-6)
+    torch.testing.assert_close(Wx.cpu(), Wr, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(dh.cpu(), dr, rtol=1e-10, atol=1e-10)
+
+
+@pytest.mark.parametrize("use_box", [True, False])
+def test_cached_forwards(cuda, use_box):
+    """Cached fixed-guide actions of the three attention installers."""
+    torch.manual_seed(4)
+    B, C, H, W, R = 2, 3, 7, 8, 1
+    x = torch.randn(B, C, H, W, dtype=torch.float64, device=cuda)
+    half = [(0, 0, False), (0, 1, True), (1, -1, True), (1, 0, True), (1, 1, True)]
+    wts = []
+    for dx, dy, _ in half:
+        w = torch.rand_like(x) + 0.1
+        if use_box:
+            w = w * O.box_mask(H, W, dx, dy, w.dtype).to(cuda)
+        wts.append(w)
+    U, D = _symmetric_serial(x.cpu(), [w.cpu() for w in wts], half, use_box)
+    from neural_shift_cuda_b200.integration import nekde_drunet_attn_patch as nk
+    cache = SimpleNamespace(C=C, shifts=half, w_fwd_list=wts, comp_box=use_box, D=None)
+    out, deg = nk._forward_cached_cuda(SimpleNamespace(), x, cache, True)
+    torch.testing.assert_close(out.cpu(), U / D, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(deg.cpu(), D, rtol=1e-10, atol=1e-10)
+
+    from neural_shift_cuda_b200.integration import nkd_metropolis_attn_patch as mp
+    cache = SimpleNamespace(C=C, shifts=half, w_hat_fwd_list=wts, comp_box=use_box,
+                            degree_hat=None)
+    Wx, dh = mp._forward_cached_cuda(SimpleNamespace(), x, cache, True)
+    torch.testing.assert_close(Wx.cpu(), x.cpu() - D * x.cpu() + U, rtol=1e-10, atol=1e-10)
+
+    from neural_shift_cuda_b200.integration import gasd_drunet_attn_patch as gp
+    full = [(dx, dy) for dx in range(-R, R + 1) for dy in range(-R, R + 1)]
+    gw = [torch.rand_like(x) + 0.1 for _ in full]
+    Kx = sum(w.cpu() * _roll(x.cpu(), dx, dy) for w, (dx, dy) in zip(gw, full))
+    Zg = sum(w.cpu() for w in gw)
+    KT = sum(torch.roll(w.cpu() * x.cpu(), shifts=(dx, dy), dims=(-2, -1))
+             for w, (dx, dy) in zip(gw, full))
+    cache = SimpleNamespace(C=C, shifts=full, w_list=gw, Z=None)
+    model = SimpleNamespace()
+    out, deg = gp._forward_cached_cuda(model, x, cache, True)
+    torch.testing.assert_close(out.cpu(), Kx / Zg, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(gp._kt_action_cached_cuda(model, x, cache).cpu(), KT,
+                               rtol=1e-10, atol=1e-10)

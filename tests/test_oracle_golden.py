@@ -95,3 +95,22 @@ def test_metropolis(name):
                                          c["gdh"])
     _close(gw, c["gw"], 1e-10, 1e-11)
     _close(gx, c["gx"], 1e-10, 1e-11)
+
+
+GOLD_NECTR = torch.load(os.path.join(os.path.dirname(__file__), "golden",
+                                     "golden_nectr.pt"), weights_only=False)
+
+
+@pytest.mark.parametrize("act", sorted(GOLD_NECTR))
+def test_nectr_model_restatement(act):
+    """The restated NECTR model 1 reproduces the reference model's serial
+    forward on the stored weights."""
+    from types import SimpleNamespace
+    from oracle.nectr_model import NECTR_denoiser
+    c = GOLD_NECTR[act]
+    m = NECTR_denoiser(SimpleNamespace(**c["args"])).double()
+    m.load_state_dict(c["state"])
+    with torch.no_grad():
+        U, Z = m(c["x"])
+    _close(U, c["U_serial"], 1e-12, 1e-12)
+    _close(Z, c["Z_serial"], 1e-12, 1e-12)
