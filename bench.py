@@ -225,7 +225,7 @@ def run_ours(args):
     else:
         def step():
             return bands.accumulate_uz_banded(x, w, sh, HG)
-        launches_per_step = 2 if R else 1
+        launches_per_step = 3 if R else 1   # band forward + two edge strips
 
     def barrier():
         if world > 1:
@@ -307,6 +307,8 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
+            "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
+                        "max": max(step_ms)},
             "clocks": clocks,
             "self_check": {"finite_and_nonnegative_Z": ok},
         }
