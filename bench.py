@@ -232,14 +232,14 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
-
     stream = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    # the clock sampler starts before the warm-up so the GPU does not idle
+    # between warm-up and the timed steps
     with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            step()
         barrier()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)

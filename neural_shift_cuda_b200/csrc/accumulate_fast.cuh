@@ -480,8 +480,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
 
     // Tile k of this CTA (ring slot k & 3), -1 when the schedule is done.
     auto tile_at = [&](uint32_t k) -> int64_t {
-        if (!dead && !mbar_try_wait(&tile_full[k & 3], (k >> 2) & 1u) &&
-            !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts)) {
+        if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts)) {
             dead = true;
             *(volatile int*)&abort_flag = 1;
         }
@@ -576,8 +575,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             auto one = [&](auto dyc, const bool second, const bool first, const bool inv) {
                 constexpr int dy = decltype(dyc)::value;
                 if (NSC_FAST_EXPERIMENT != 2 && !second && !dead) {
-                    if (!mbar_try_wait(&full[stage], phase) &&
-                        !mbar_wait(&full[stage], phase, timeouts)) {
+                    if (!mbar_wait(&full[stage], phase, timeouts)) {
                         dead = true;
                         *(volatile int*)&abort_flag = 1;
                     }

@@ -3,7 +3,7 @@
 //
 // No load here uses cluster multicast: every tensor copy reads this GPU's
 // own memory into this CTA's shared memory.  Every wait on an mbarrier is
-// bounded (kWaitLimit polls); a wait that gives up bumps a device counter
+// bounded (kSleepWaits hinted waits); a wait that gives up bumps a device counter
 // (see wait_timeout_counter) and the caller unwinds instead of hanging.
 #pragma once
 
@@ -13,7 +13,6 @@
 
 namespace nsc {
 
-constexpr uint32_t kWaitLimit = 1u << 26;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -53,12 +52,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase of `parity` to complete.  Returns false (and
-// counts a timeout) when the poll budget runs out.
+// try_wait with a suspend-time hint: a waiting warp is parked by the
+// hardware until the phase completes or the hint (1 ms) expires, instead of
+// spinning and taking issue slots from the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok)
+                 : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+                 : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase of `parity` to complete: at most
+// kSleepWaits hinted waits (seconds in total).  Returns false (and counts a
+// timeout) when the budget runs out.
+constexpr uint32_t kSleepWaits = 4096;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           unsigned int* timeouts) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t i = 0; i < kSleepWaits; ++i)
+        if (mbar_try_wait_sleep(bar, parity)) return true;
     atomicAdd(timeouts, 1u);
     return false;
 }
