@@ -118,7 +118,7 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
             if (e < 0) continue;
             const int mo = dy > 0 ? (dy + V - 1) / V * V : 0;
             const int pmo = prev_dy > 0 ? (prev_dy + V - 1) / V * V : 0;
-            if (prev >= 0) {
+            if (prev >= 0 && NSC_FAST_PAIRS) {
                 int16_t& pe = tab.s[dx + MAXR][prev_dy + MAXR];
                 if (!(pe & (kPairFirst | kPairSecond)) && (e & kSMask) == (pe & kSMask) + 1 &&
                     mo == pmo) {
@@ -151,8 +151,8 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
             const bool inv = e & kInvBit;
             const bool first = e & kPairFirst, second = e & kPairSecond;
             const bool want_inv = dy > 0 || dx != 0;
-            const bool want_first = dy > 0 && (dy & 1) && dy < rx;
-            const bool want_second = dy > 0 && !(dy & 1);
+            const bool want_first = NSC_FAST_PAIRS && dy > 0 && (dy & 1) && dy < rx;
+            const bool want_second = NSC_FAST_PAIRS && dy > 0 && !(dy & 1);
             if (inv != want_inv || first != want_first || second != want_second) {
                 exact = false;
                 break;

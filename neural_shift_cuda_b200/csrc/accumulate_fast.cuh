@@ -37,9 +37,14 @@
 // Build-time switch for throughput experiments (0 in every shipped build):
 // 1 = stream the weights without the arithmetic, 2 = arithmetic without
 // waiting for the weights, 3 = as 1 and without staging x, 4 = arithmetic
-// only: no weight copies, no waits.
+// only: no weight copies, no waits, 6 = arithmetic only, static tile order,
+// no barriers at all.
 #ifndef NSC_FAST_EXPERIMENT
 #define NSC_FAST_EXPERIMENT 0
+#endif
+// 1: two consecutive shifts share one weight copy (canonical tables)
+#ifndef NSC_FAST_PAIRS
+#define NSC_FAST_PAIRS 1
 #endif
 
 #include "nsc_common.cuh"
@@ -370,7 +375,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
 
     // ------------------------------------------------------------ producer
     if (tid >= NCONS) {
-        if (tid != NCONS) return;
+        if (tid != NCONS || NSC_FAST_EXPERIMENT == 6) return;
         uint32_t it = 0;
         int stage = 0;
         uint32_t phase = 0;
@@ -480,6 +485,10 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
 
     // Tile k of this CTA (ring slot k & 3), -1 when the schedule is done.
     auto tile_at = [&](uint32_t k) -> int64_t {
+        if (NSC_FAST_EXPERIMENT == 6) {
+            const int64_t t = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+            return t < g.ntiles ? t : -1;
+        }
         if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts)) {
             dead = true;
             *(volatile int*)&abort_flag = 1;
@@ -574,7 +583,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             uint32_t stp = stages32 + stage * g.stage_stride;
             auto one = [&](auto dyc, const bool second, const bool first, const bool inv) {
                 constexpr int dy = decltype(dyc)::value;
-                if (NSC_FAST_EXPERIMENT != 2 && !second && !dead) {
+                if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && !second && !dead) {
                     if (!mbar_wait(&full[stage], phase, timeouts)) {
                         dead = true;
                         *(volatile int*)&abort_flag = 1;
@@ -613,7 +622,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 }
                 if (!first) {   // copy fully used: release it
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[stage]);
+                    if (lane == 0 && NSC_FAST_EXPERIMENT != 6) mbar_arrive(&empty[stage]);
                     if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
                     stp = stages32 + stage * g.stage_stride;
                 }
@@ -627,7 +636,9 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 static_for<1, DYMAX + 1>([&](auto jc) {
                     constexpr int dy = decltype(jc)::value;
                     if (dy > R) return;
-                    if constexpr (dy & 1)
+                    if constexpr (!NSC_FAST_PAIRS)
+                        one(jc, false, false, true);
+                    else if constexpr (dy & 1)
                         one(jc, false, dy < R, true);
                     else
                         one(jc, true, false, true);
