@@ -46,6 +46,10 @@
 #ifndef NSC_FAST_PAIRS
 #define NSC_FAST_PAIRS 1
 #endif
+// x halo tile buffers: 2 = the next tile's x is prefetched during this one
+#ifndef NSC_FAST_XBUF
+#define NSC_FAST_XBUF 2
+#endif
 
 #include "nsc_common.cuh"
 #include "nsc_tma.cuh"
@@ -347,7 +351,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
     T* xa0 = reinterpret_cast<T*>(smem + NSTAGE * g.stage_stride);
     const int xtile = NC * g.XH * g.XW;
     uint64_t* full = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(xa0 + 2 * xtile) + 15) & ~uintptr_t(15));
+        (reinterpret_cast<uintptr_t>(xa0 + NSC_FAST_XBUF * xtile) + 15) & ~uintptr_t(15));
     uint64_t* empty = full + NSTAGE;
     // Dynamic tile order: the producer draws tickets from a global counter
     // (two tiles ahead) and publishes them in a 4-slot ring.  Tiles are then
@@ -438,6 +442,8 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
     }
 
     // ------------------------------------------------------------ consumers
+    const uint32_t stages32 = smem_u32(stages);
+    const uint32_t full32 = smem_u32(full), empty32 = smem_u32(empty);
     const int tr = tid / TPR, tc = tid % TPR;
     const int lane = tid & 31;
     int stage = 0;
@@ -503,6 +509,10 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         const int64_t b = id.b;
         const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
         const int h0 = id.h0, w0 = id.w0;
+        if (NSC_FAST_XBUF == 1 && k > 0) {
+            named_sync(1, NCONS);   // every thread is done with the previous tile
+            if (NSC_FAST_EXPERIMENT != 3) issue_x(tile, xa0);
+        }
         T* xa = xa0 + buf * xtile;
         const bool row_border = h0 - Rx < 0 || h0 + TH + Rx > g.H;
         const bool col_border = w0 - XC < 0 || w0 + TW + XC + V > g.W;
@@ -531,7 +541,8 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
         }
         // prefetch the next tile's x while this one computes
         const int64_t next = tile_at(k + 1);
-        if (NSC_FAST_EXPERIMENT != 3 && next >= 0) issue_x(next, xa0 + (buf ^ 1) * xtile);
+        if (NSC_FAST_XBUF == 2 && NSC_FAST_EXPERIMENT != 3 && next >= 0)
+            issue_x(next, xa0 + (buf ^ 1) * xtile);
 
         float u[NC][V], z[V];
 #pragma unroll
@@ -579,17 +590,17 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             const uint32_t off_mir = static_cast<uint32_t>(((mrow0 - dx) * BW + tc * V) * sizeof(T));
             const uint64_t m_pres = tab.present[dx + MAXR], m_inv = tab.inv[dx + MAXR];
             const uint64_t m_first = tab.first[dx + MAXR], m_second = tab.second[dx + MAXR];
-            const uint32_t stages32 = smem_u32(stages);
             uint32_t stp = stages32 + stage * g.stage_stride;
+            uint32_t stp2 = stp + g.plane_bytes;
             auto one = [&](auto dyc, const bool second, const bool first, const bool inv) {
                 constexpr int dy = decltype(dyc)::value;
                 if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && !second && !dead) {
-                    if (!mbar_wait(&full[stage], phase, timeouts)) {
+                    if (!mbar_wait32(full32 + 8 * stage, phase, timeouts)) {
                         dead = true;
                         *(volatile int*)&abort_flag = 1;
                     }
                 }
-                const uint32_t sp = after(stp + (second ? g.plane_bytes : 0u));
+                const uint32_t sp = after(second ? stp2 : stp);
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
                 lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
@@ -622,9 +633,15 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 }
                 if (!first) {   // copy fully used: release it
                     __syncwarp();
-                    if (lane == 0 && NSC_FAST_EXPERIMENT != 6) mbar_arrive(&empty[stage]);
-                    if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-                    stp = stages32 + stage * g.stage_stride;
+                    if (lane == 0 && NSC_FAST_EXPERIMENT != 6) mbar_arrive32(empty32 + 8 * stage);
+                    if (++stage == NSTAGE) {
+                        stage = 0;
+                        phase ^= 1u;
+                        stp = stages32;
+                    } else {
+                        stp += g.stage_stride;
+                    }
+                    stp2 = stp + g.plane_bytes;
                 }
             };
             if constexpr (EXACT) {
@@ -670,7 +687,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 }
             }
         }
-        buf ^= 1;
+        if (NSC_FAST_XBUF == 2) buf ^= 1;
         tile = next;
     }
     cp_async_wait_all();

@@ -25,7 +25,8 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
     }
     // ring depth: as many weight stages (<= 12) as fit next to the two
     // x tiles in the 227 KB a CTA may use
-    const size_t fixed = 2ull * NC * g.XH * g.XW * sizeof(T) + 16 + 4 * 16 + 16 + 128;
+    const size_t fixed = static_cast<size_t>(NSC_FAST_XBUF) * NC * g.XH * g.XW * sizeof(T) +
+                         16 + 4 * 16 + 16 + 128;
     const size_t per_stage = g.stage_stride + 2 * sizeof(uint64_t);
     const size_t cap = 227u * 1024u;
     if (fixed + 3 * per_stage > cap) {

@@ -66,6 +66,29 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
     return ok != 0;
 }
 
+// The same waits by 32-bit shared address (no generic-to-shared conversion).
+__device__ __forceinline__ bool mbar_try_wait32(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_try_wait_sleep32(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity), "r"(1000000u) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive32(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\t"
+                 "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+                 : "memory");
+}
+
 // Bounded wait for the phase of `parity` to complete: at most
 // kSleepWaits hinted waits (seconds in total).  Returns false (and counts a
 // timeout) when the budget runs out.
@@ -75,6 +98,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < kSleepWaits; ++i)
         if (mbar_try_wait_sleep(bar, parity)) return true;
+    atomicAdd(timeouts, 1u);
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait32(uint32_t bar, uint32_t parity,
+                                            unsigned int* timeouts) {
+    if (mbar_try_wait32(bar, parity)) return true;
+    for (uint32_t i = 0; i < kSleepWaits; ++i)
+        if (mbar_try_wait_sleep32(bar, parity)) return true;
     atomicAdd(timeouts, 1u);
     return false;
 }
