@@ -382,6 +382,328 @@ def run_e2e(args, x, w, sh, world, dev):
             "steps": steps, "pinned": pinned, "ms_per_step": ms}
 
 
+# ---------------------------------------------------------------------------
+# Secondary workloads (BASELINE.json configs[1..3]): one op per step,
+# batch-sharded across ranks (images are independent: no collective).
+# ---------------------------------------------------------------------------
+
+class OpWorkload:
+    """One op of the path on one BASELINE configuration.
+
+    make(dev, b0, nb) -> dict(inputs=[device tensors], run=callable(*inputs)
+    -> outputs, launches=int, units=pixel-shifts of the nb images);
+    `cpu(nb)` runs the oracle on a bounded slice and returns (units, seconds,
+    description)."""
+
+    def __init__(self, name, metric, B, config, dtype, make, cpu):
+        self.name, self.metric, self.B = name, metric, B
+        self.config, self.dtype, self.make, self.cpu = config, dtype, make, cpu
+
+
+def _seeded(shape, b0, nb, seed, dev, fn):
+    """Rows b0..b0+nb of a batch tensor whose images are seeded one by one,
+    so any batch split sees the same data."""
+    out = []
+    for b in range(b0, b0 + nb):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1009 + b)
+        out.append(fn(g, shape))
+    return torch.stack(out, 0)
+
+
+def _wl_pair_gather():
+    Bt, Cg, Hs, Ws, Rr = 8, 16, 256, 256, 5
+    rows = halfplane(Rr)
+
+    def make(dev, b0, nb):
+        import neural_shift_cuda_b200 as nsc
+        guide = _seeded((Cg, Hs, Ws), b0, nb, 1, dev,
+                        lambda g, sh: torch.rand(sh, generator=g, device=dev))
+        sh = torch.tensor(rows)
+        return dict(inputs=[guide], run=lambda gd: nsc.pair_gather(gd, sh),
+                    launches=1, units=len(rows) * nb * 2 * Cg * Hs * Ws)
+
+    def cpu(nb):
+        from oracle import nsc_oracle as O
+        g = torch.Generator().manual_seed(0)
+        guide = torch.rand(nb, Cg, Hs, Ws, generator=g)
+        t0 = time.perf_counter()
+        O.pair_gather(guide, torch.tensor(rows))
+        return (len(rows) * nb * 2 * Cg * Hs * Ws, time.perf_counter() - t0,
+                f"oracle pair_gather on {nb} of {Bt} images")
+
+    return OpWorkload(
+        "pair_gather", "pixel-shifts/s (pair_gather fwd, NECTR configs[1]: "
+        "guide (8,16,256,256) f32, R=5 S=61)", Bt,
+        {"workload": "pair_gather fwd, NECTR latent guide (8,16,256,256) f32, "
+                     "half-plane R=5 S=61 (configs[1])"},
+        "f32 copy", make, cpu)
+
+
+def _wl_normalized():
+    Bt, Cx, Hs, Ws, Rr = 16, 3, 512, 512, 7
+    rows = [(dx, dy, 0) for dx in range(-Rr, Rr + 1) for dy in range(-Rr, Rr + 1)]
+    Sn = len(rows)
+
+    def make(dev, b0, nb):
+        import neural_shift_cuda_b200 as nsc
+        x = _seeded((Cx, Hs, Ws), b0, nb, 2, dev,
+                    lambda g, sh: torch.rand(sh, generator=g, device=dev)
+                    ).to(torch.bfloat16)
+        # logits N(0, 3^2), batch-major (B, S, H, W) as the attention
+        # produces them, handed over shift-major and channel-broadcast
+        lg = _seeded((Sn, Hs, Ws), b0, nb, 3, dev,
+                     lambda g, sh: 3.0 * torch.randn(sh, generator=g, device=dev)
+                     ).to(torch.bfloat16)
+        lg = lg.transpose(0, 1).reshape(Sn * nb, 1, Hs, Ws).contiguous()
+        sh = torch.tensor(rows)
+        return dict(inputs=[x, lg],
+                    run=lambda a, b: nsc.normalized_accumulate_uz(
+                        a, b.expand(-1, Cx, -1, -1), sh, log_weights=True,
+                        return_log_degree=True, validate=False),
+                    launches=1, units=Sn * nb * Cx * Hs * Ws)
+
+    def cpu(nb):
+        from oracle import nsc_oracle as O
+        g = torch.Generator().manual_seed(0)
+        rows_s = 64
+        x = torch.rand(1, Cx, rows_s, Ws, generator=g).to(torch.bfloat16)
+        lg = (3.0 * torch.randn(Sn, 1, rows_s, Ws, generator=g)).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        O.normalized_accumulate_uz(x, lg.expand(-1, Cx, -1, -1), torch.tensor(rows),
+                                   log_weights=True)
+        return (Sn * Cx * rows_s * Ws, time.perf_counter() - t0,
+                f"oracle normalized_accumulate_uz (log) on a (1,3,{rows_s},512) band, S={Sn}")
+
+    return OpWorkload(
+        "normalized", "pixel-shifts/s (normalized_accumulate_uz fwd, log weights, "
+        "GASD configs[2]: x bf16 (16,3,512,512), S=225)", Bt,
+        {"workload": "normalized_accumulate_uz fwd, logits N(0,9) bf16 channel-"
+                     "shared, full window R=7 S=225, x bf16 (16,3,512,512) (configs[2])"},
+        "bf16 in, f32 accumulate", make, cpu)
+
+
+def _wl_metropolis():
+    Bt, Cx, Hs, Ws, Rr = 16, 3, 512, 512, 5
+    rows = halfplane(Rr)
+    Sm = len(rows)
+
+    def make(dev, b0, nb):
+        from neural_shift_cuda_b200.metropolis import metropolis_aggregate
+        x = _seeded((Cx, Hs, Ws), b0, nb, 4, dev,
+                    lambda g, sh: torch.rand(sh, generator=g, device=dev))
+        wh = _seeded((Sm, 1, Hs, Ws), b0, nb, 5, dev,
+                     lambda g, sh: torch.sigmoid(torch.randn(sh, generator=g, device=dev)))
+        gw = _seeded((Cx, Hs, Ws), b0, nb, 6, dev,
+                     lambda g, sh: torch.randn(sh, generator=g, device=dev))
+        sh = torch.tensor(rows)
+
+        def run(w, xi, gy):
+            w = w.detach().requires_grad_(True)
+            xi = xi.detach().requires_grad_(True)
+            Wx, dh = metropolis_aggregate(w.expand(-1, -1, Cx, -1, -1), xi, sh,
+                                          use_box=True, eps=1e-6)
+            gwh, gx = torch.autograd.grad(Wx, (w, xi), gy)
+            return Wx, gwh, gx
+        return dict(inputs=[wh, x, gw], run=run, launches=2,
+                    units=2 * Sm * nb * Cx * Hs * Ws)
+
+    def cpu(nb):
+        from oracle import nsc_oracle as O
+        g = torch.Generator().manual_seed(0)
+        rows_s = 64
+        x = torch.rand(1, Cx, rows_s, Ws, generator=g)
+        wh = torch.sigmoid(torch.randn(1, Sm, 1, rows_s, Ws, generator=g))
+        gy = torch.randn(1, Cx, rows_s, Ws, generator=g)
+        t0 = time.perf_counter()
+        O.metropolis_aggregate_grad(wh, x, torch.tensor(rows), True, 1e-6, gy,
+                                    torch.zeros_like(gy))
+        return (2 * Sm * Cx * rows_s * Ws, time.perf_counter() - t0,
+                f"oracle metropolis_aggregate fwd+bwd (autograd) on a (1,3,{rows_s},512) band, S={Sm}")
+
+    return OpWorkload(
+        "metropolis", "pixel-shifts/s (metropolis_aggregate fwd+bwd, NKD_mp "
+        "configs[3]: x f32 (16,3,512,512), S=61)", Bt,
+        {"workload": "metropolis_aggregate fwd+bwd, w_half sigmoid(N(0,1)) "
+                     "(16,61,1,512,512) f32 broadcast over C=3, use_box, R=5 S=61 "
+                     "(configs[3])"},
+        "f32", make, cpu)
+
+
+WORKLOADS = {"pair_gather": _wl_pair_gather, "normalized": _wl_normalized,
+             "metropolis": _wl_metropolis}
+
+
+def _nbytes(ts):
+    out = 0
+    for t in ts:
+        if isinstance(t, torch.Tensor):
+            out += t.numel() * t.element_size()
+        elif isinstance(t, (tuple, list)):
+            out += _nbytes(t)
+    return out
+
+
+def run_workload(args, wl):
+    """Time one secondary workload: the batch is split across ranks; value =
+    pixel-shifts of the whole batch / max-over-ranks time."""
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        vals = []
+        for i in range(args.warmup + args.steps):
+            u, dt, desc = wl.cpu(1)
+            if i >= args.warmup:
+                vals.append(u / dt)
+        v = statistics.median(vals)
+        threads = torch.get_num_threads()
+        print(json.dumps({
+            "impl": "reference", "metric": wl.metric, "value": v, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": wl.dtype, "data": "synthetic", "config": wl.config,
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads,
+                             "kind": "port", "sample": desc},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    nb = wl.B // world + (1 if rank < wl.B % world else 0)
+    b0 = rank * (wl.B // world) + min(rank, wl.B % world)
+    w = wl.make(dev, b0, nb)
+    inputs, run = w["inputs"], w["run"]
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("warmup")
+        for _ in range(args.warmup):
+            out = run(*inputs)
+        torch.cuda.nvtx.range_pop()
+        del out
+        barrier()
+        t0, t1 = (torch.cuda.Event(enable_timing=True),
+                  torch.cuda.Event(enable_timing=True))
+        torch.cuda.nvtx.range_push("timed")
+        t0.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            out = run(*inputs)
+            ev[i][1].record(stream)
+            if i + 1 < args.steps:
+                del out
+        t1.record(stream)
+        torch.cuda.nvtx.range_pop()
+        barrier()
+    total = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total = float(t.item())
+    ms = total / args.steps
+    units_all = w["units"] * wl.B // max(nb, 1) if world == 1 else None
+    if world > 1:
+        u = torch.tensor([float(w["units"])], device=dev, dtype=torch.float64)
+        dist.all_reduce(u)
+        units_all = u.item()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    kern_ms = statistics.median(step_ms)
+    alg = _nbytes(inputs) + _nbytes(out)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = alg / (kern_ms * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        hin = []
+        for t in inputs:
+            try:
+                h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            except RuntimeError:
+                h = torch.empty(t.shape, dtype=t.dtype)
+            h.copy_(t)
+            hin.append(h)
+        outs = [o for o in (out if isinstance(out, (tuple, list)) else [out])]
+        hout = [torch.empty(o.shape, dtype=o.dtype, pin_memory=hin[0].is_pinned())
+                for o in outs]
+        din = [torch.empty_like(t) for t in inputs]
+
+        def once():
+            for d, h in zip(din, hin):
+                d.copy_(h, non_blocking=True)
+            res = run(*din)
+            res = res if isinstance(res, (tuple, list)) else [res]
+            for h, o in zip(hout, res):
+                h.copy_(o, non_blocking=True)
+        once()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(1, min(args.steps, args.e2e_steps))
+        a.record()
+        for _ in range(n):
+            once()
+        b.record()
+        torch.cuda.synchronize()
+        e_ms = a.elapsed_time(b) / n
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": units_all / (e_ms * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": _nbytes(hin) * world,
+               "d2h_bytes_per_step": _nbytes(hout) * world, "steps": n,
+               "ms_per_step": e_ms}
+    clocks = clk.summary()
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu and world == 1:
+            torch.set_num_threads(os.cpu_count() or 1)
+            wl.cpu(1)
+            u, dt, desc = wl.cpu(1)
+            cpu = {"value": u / dt, "unit": UNIT, "cores": torch.get_num_threads(),
+                   "kind": "port", "sample": desc}
+        cfg = dict(wl.config)
+        cfg.update({"B": wl.B, "parallelism": f"batch shards x{world}" if world > 1
+                    else "single GPU", "l2": "inputs larger than L2" if
+                    _nbytes(inputs) > 126e6 else "inputs smaller than L2"})
+        print(json.dumps({
+            "metric": wl.metric, "value": units_all / (ms * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+            "config": cfg,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                         "kernel_ms": kern_ms, "algorithmic_bytes": alg,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
+                         if peaks else "fallback 6650 GB/s",
+                         "note": "step time of all launches of the op (per rank)"},
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": w["launches"] * args.steps,
+            "step_ms": {"min": min(step_ms), "median": kern_ms, "max": max(step_ms)},
+            "clocks": clocks}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -395,7 +717,14 @@ def main():
     ap.add_argument("--size", type=int, default=8192,
                     help="image side (8192 is the benchmark; smaller sides "
                          "are for profiling captures only)")
+    ap.add_argument("--workload", default="accumulate",
+                    choices=["accumulate"] + sorted(WORKLOADS),
+                    help="accumulate (configs[4], the headline) or one of the "
+                         "secondary op workloads of configs[1..3]")
     args = ap.parse_args()
+    if args.workload != "accumulate":
+        run_workload(args, WORKLOADS[args.workload]())
+        return
     global HG, WG, PIXEL_SHIFTS
     HG = WG = args.size
     PIXEL_SHIFTS = S * B * C * HG * WG

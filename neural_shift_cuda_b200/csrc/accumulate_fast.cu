@@ -181,6 +181,10 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     const int XC = align_up(K, V);
     g.BH = TH + rx;
     g.BW = TW + XC;
+#ifdef NSC_FAST_BOX_PROBE   // throughput probe only (wrong results): smaller boxes
+    if (NSC_FAST_BOX_PROBE & 1) g.BH = TH;
+    if (NSC_FAST_BOX_PROBE & 2) g.BW = TW;
+#endif
     g.stage_tx = static_cast<uint32_t>(g.BH) * g.BW * es;
     g.stage_stride = (g.stage_tx + 127u) & ~127u;
     g.XH = TH + 2 * rx;

@@ -64,7 +64,10 @@ constexpr int TPR = 16;         // threads per row
 constexpr int NCONS = TH * TPR; // consumer threads
 constexpr int NTHREADS = NCONS + 32;
 constexpr int MAXSTAGE = 16;     // ring depth is chosen per launch (<= this)
-constexpr int STRIP = 8;        // tile columns per raster strip
+#ifndef NSC_FAST_STRIP
+#define NSC_FAST_STRIP 8
+#endif
+constexpr int STRIP = NSC_FAST_STRIP;   // tile columns per raster strip
 constexpr int MAXR = 16;        // |dx|, |dy| <= MAXR on this path
 constexpr int kInvBit = 0x800;       // row has a mirror term
 constexpr int kPairFirst = 0x1000;   // shares its weight copy with the next entry
@@ -159,6 +162,12 @@ __device__ __forceinline__ void fma_e(float& acc, const uint32_t* w, const uint3
         acc = fmaf(__uint_as_float(w[WI]), __uint_as_float(x[XI]), acc);
     } else {
         const uint32_t ww = w[WI >> 1], xx = x[XI >> 1];
+#ifdef NSC_FAST_FMA_PROBE   // throughput probe only: fp32 FMA on the raw words
+        if constexpr (true) {
+            acc = fmaf(__uint_as_float(ww), __uint_as_float(xx), acc);
+            return;
+        }
+#endif
 #if NSC_FAST_EXPERIMENT == 5
         constexpr int sel = 0;   // throughput probe only: wrong results
 #else
@@ -193,6 +202,12 @@ __device__ __forceinline__ void add_e(float& acc, const uint32_t* w) {
         acc += __uint_as_float(w[WI]);
     } else {
         const uint32_t ww = w[WI >> 1];
+#ifdef NSC_FAST_FMA_PROBE
+        if constexpr (true) {
+            acc += __uint_as_float(ww);
+            return;
+        }
+#endif
         if constexpr (Elem<T>::kind == 0) {
             if constexpr ((WI & 1) == 0)
                 asm("{.reg .b16 a0,a1; mov.b32 {a0,a1},%1; add.f32.f16 %0, a0, %0;}" : "+f"(acc) : "r"(ww));

@@ -16,6 +16,8 @@
 // backward scatters with atomicAdd (shift_ops_cuda.cu:206-246); this one is
 // deterministic.
 
+#include <cstdlib>
+
 #include "nsc_common.cuh"
 #include "nsc_host.h"
 
@@ -78,6 +80,101 @@ gather_fwd_kernel(const E* __restrict__ guide, E* __restrict__ out,
     }
 }
 
+// Tiled forward.  One CTA owns a TH x TW tile of one guide plane (b, c):
+// it stages the tile plus its (Rx, Ry) halo -- rows and columns wrapped
+// circularly -- in shared memory once, then writes the tile of every
+// output plane that reads it: the S shifted copies, the S centre copies of
+// pair_gather, and (channel 0 only) the S mask tiles.  Each thread writes
+// one 16-byte vector per row with a streaming store (the S-fold output is
+// written once and never re-read here, so it must not evict the guide from
+// L2).  HBM sees the output once and the guide about once.
+constexpr int kTileRows = 16;
+
+__device__ __forceinline__ int pmod32(int a, int n) {
+    const int r = a % n;
+    return r < 0 ? r + n : r;
+}
+
+template <typename E, int V>
+__global__ void __launch_bounds__(kThreads)
+gather_tile_kernel(const E* __restrict__ guide, E* __restrict__ out,
+                   E* __restrict__ mask, const ShiftTable st, int B, int C,
+                   int H, int W, int pair, E one, int Rx, int Ry,
+                   int tiles_x, int64_t ntiles, int64_t planes) {
+    constexpr int TW = 32 * V;
+    using Vec16 = Vec<E, V>;
+    extern __shared__ __align__(16) unsigned char smem_g[];
+    E* xs = reinterpret_cast<E*>(smem_g);
+    const int XP = TW + 2 * Ry;          // halo row pitch (elements)
+    const int XR = kTileRows + 2 * Rx;   // halo rows
+    const int tid = threadIdx.x;
+    const int lx = tid & 31, ly = tid >> 5;
+    const int Cout = pair ? 2 * C : C;
+    const int64_t HW = static_cast<int64_t>(H) * W;
+    for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
+        const int b = static_cast<int>(plane / C);
+        const int c = static_cast<int>(plane - static_cast<int64_t>(b) * C);
+        const E* src = guide + plane * HW;
+        for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            const int ty = static_cast<int>(tile / tiles_x);
+            const int tx = static_cast<int>(tile - static_cast<int64_t>(ty) * tiles_x);
+            const int h0 = ty * kTileRows, w0 = tx * TW;
+            __syncthreads();   // previous tile's readers are done
+            for (int idx = tid; idx < XR * XP; idx += kThreads) {
+                const int i = idx / XP;
+                const int j = idx - i * XP;
+                const int r = pmod32(h0 - Rx + i, H);
+                const int col = pmod32(w0 - Ry + j, W);
+                xs[idx] = __ldg(src + static_cast<int64_t>(r) * W + col);
+            }
+            __syncthreads();
+            const int wc = w0 + lx * V;
+            // centre vectors of this thread's rows (pair_gather)
+            Vec16 ctr[kTileRows / 8];
+#pragma unroll
+            for (int p = 0; p < kTileRows / 8; ++p) {
+                const int r = p * 8 + ly;
+#pragma unroll
+                for (int i = 0; i < V; ++i) ctr[p].v[i] = xs[(r + Rx) * XP + Ry + lx * V + i];
+            }
+            for (int s = 0; s < st.S; ++s) {
+                const int dx = st.dx[s], dy = st.dy[s];
+                const int64_t sb = static_cast<int64_t>(s) * B + b;
+                E* dsh = out + (sb * Cout + (pair ? C + c : c)) * HW;
+                E* dce = out + (sb * Cout + c) * HW;
+                E* dm = mask + sb * HW;
+#pragma unroll
+                for (int p = 0; p < kTileRows / 8; ++p) {
+                    const int r = p * 8 + ly;
+                    const int h = h0 + r;
+                    if (h >= H || wc >= W) continue;
+                    const int64_t o = static_cast<int64_t>(h) * W + wc;
+                    Vec16 v;
+                    const E* row = xs + (r + dx + Rx) * XP + Ry + lx * V + dy;
+#pragma unroll
+                    for (int i = 0; i < V; ++i) v.v[i] = row[i];
+                    __stcs(reinterpret_cast<uint4*>(dsh + o),
+                           *reinterpret_cast<const uint4*>(&v));
+                    if (pair)
+                        __stcs(reinterpret_cast<uint4*>(dce + o),
+                               *reinterpret_cast<const uint4*>(&ctr[p]));
+                    if (c == 0) {
+                        const bool hv = h + dx >= 0 && h + dx < H;
+                        Vec16 m;
+#pragma unroll
+                        for (int i = 0; i < V; ++i) {
+                            const int q = wc + i + dy;
+                            m.v[i] = (hv && q >= 0 && q < W) ? one : E(0);
+                        }
+                        __stcs(reinterpret_cast<uint4*>(dm + o),
+                               *reinterpret_cast<const uint4*>(&m));
+                    }
+                }
+            }
+        }
+    }
+}
+
 // Backward: grad_guide(b, c, g) = sum_s go_shift(s, b, c, g - d_s) [+ the
 // centre half go(s, b, c, g) for pair_gather].
 template <typename T>
@@ -124,6 +221,41 @@ void launch_fwd(const void* guide, void* out, void* mask, const ShiftTable& st,
         st, B, C, H, W, pair, one, planes, units);
 }
 
+// The tiled path: 16-byte aligned rows, halo within 32 rows / 64 columns,
+// per-dimension extents below 2^31 (intra-plane int32 indexing).
+template <typename E>
+bool launch_tile(const void* guide, void* out, void* mask, const ShiftTable& st,
+                 int64_t B, int64_t C, int64_t H, int64_t W, int pair, E one,
+                 cudaStream_t stream) {
+    constexpr int V = 16 / sizeof(E);
+    constexpr int TW = 32 * V;
+    if (H >= (1LL << 30) || W >= (1LL << 30) || B * C * 2 >= (1LL << 30)) return false;
+    int Rx = 0, Ry = 0;
+    for (int s = 0; s < st.S; ++s) {
+        Rx = st.dx[s] < 0 ? (-st.dx[s] > Rx ? -st.dx[s] : Rx) : (st.dx[s] > Rx ? st.dx[s] : Rx);
+        Ry = st.dy[s] < 0 ? (-st.dy[s] > Ry ? -st.dy[s] : Ry) : (st.dy[s] > Ry ? st.dy[s] : Ry);
+    }
+    if (Rx > 32 || Ry > 64) return false;
+    Ry = (Ry + V - 1) / V * V;   // keeps the centre vectors 16-byte aligned
+    const size_t smem = static_cast<size_t>(kTileRows + 2 * Rx) * (TW + 2 * Ry) * sizeof(E);
+    if (smem > 96 * 1024) return false;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(gather_tile_kernel<E, V>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return false;
+    const int tiles_x = static_cast<int>((W + TW - 1) / TW);
+    const int64_t ntiles = static_cast<int64_t>(tiles_x) * ((H + kTileRows - 1) / kTileRows);
+    const int64_t planes = B * C;
+    const unsigned gx = static_cast<unsigned>(ntiles < (1LL << 31) - 1 ? ntiles : (1LL << 31) - 1);
+    const unsigned gy = static_cast<unsigned>(planes < 65535 ? planes : 65535);
+    gather_tile_kernel<E, V><<<dim3(gx, gy), kThreads, smem, stream>>>(
+        static_cast<const E*>(guide), static_cast<E*>(out), static_cast<E*>(mask), st,
+        static_cast<int>(B), static_cast<int>(C), static_cast<int>(H),
+        static_cast<int>(W), pair, one, Rx, Ry, tiles_x, ntiles, planes);
+    return true;
+}
+
 template <typename E>
 void dispatch_fwd(const void* guide, void* out, void* mask, const ShiftTable& st,
                   int64_t B, int64_t C, int64_t H, int64_t W, int pair, E one,
@@ -132,6 +264,9 @@ void dispatch_fwd(const void* guide, void* out, void* mask, const ShiftTable& st
     const bool aligned = (W % V == 0) &&
                          (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(mask) % 16 == 0);
+    if (aligned && !getenv("NSC_GATHER_GENERIC") &&
+        launch_tile<E>(guide, out, mask, st, B, C, H, W, pair, one, stream))
+        return;
     if (aligned)
         launch_fwd<E, V>(guide, out, mask, st, B, C, H, W, pair, one, stream);
     else

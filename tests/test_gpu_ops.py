@@ -62,6 +62,28 @@ def test_gathers_other_dtypes(cuda, dtype):
     assert torch.equal(out.cpu(), ro) and torch.equal(mask.cpu(), rm)
 
 
+@pytest.mark.parametrize("generic", [False, True])
+@pytest.mark.parametrize("dtype,shape,rows", [
+    (torch.float32, (2, 3, 37, 300), [(3, -5, 1), (-2, 7, 0), (0, 0, 1)]),
+    (torch.float16, (1, 2, 5, 64), [(4, 9, 1), (-5, -3, 0), (5, 64, 1)]),
+    (torch.bfloat16, (2, 1, 40, 520), [(dx, dy, 1) for dx in (-7, 0, 7) for dy in (-9, 1, 9)]),
+    (torch.float64, (1, 2, 20, 18), [(1, 1, 1), (-3, 2, 0)]),
+    (torch.float32, (1, 1, 64, 128), [(40, 3, 1), (0, -70, 1)]),   # halo too large: general kernel
+])
+def test_gathers_tiled_and_general(cuda, generic, dtype, shape, rows, monkeypatch):
+    """Both forward kernels (halo-tiled and one-vector-per-thread) on ragged
+    tiles, tiny planes (shifts wrapping more than a tile), every dtype."""
+    if generic:
+        monkeypatch.setenv("NSC_GATHER_GENERIC", "1")
+    torch.manual_seed(2)
+    g = torch.randn(*shape).to(dtype)
+    sh = T(rows)
+    for fn, ref in ((nsc.shift_gather, O.shift_gather), (nsc.pair_gather, O.pair_gather)):
+        out, mask = fn(g.to(cuda), sh)
+        ro, rm = ref(g, sh)
+        assert torch.equal(out.cpu(), ro) and torch.equal(mask.cpu(), rm)
+
+
 @pytest.mark.parametrize("pair", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
 def test_gather_backward(cuda, pair, dtype):
