@@ -20,6 +20,7 @@
 #include <cmath>
 
 #include "nsc_common.cuh"
+#include "normalized_fast.h"
 #include "nsc_host.h"
 
 namespace nsc {
@@ -301,6 +302,12 @@ nsc_status nsc_normalized_accumulate_uz_fwd(
     if (!x || !w || !D || !log_C)
         return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
     cudaStream_t sm = as_stream(stream);
+    if (norm_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, st,
+                      log_weights ? 1 : 0, D, log_C, invalid_flag, sm))
+        return check_launch(op);
+    if (getenv("NSC_REQUIRE_FAST"))
+        return fail(NSC_ERR_INVALID_ARG, "%s: tiled path declined: %s", op,
+                    norm_fast_decline_reason());
     return with_types(op, x_dtype, w_dtype, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
