@@ -501,8 +501,9 @@ def _wl_metropolis():
         def run(w, xi, gy):
             w = w.detach().requires_grad_(True)
             xi = xi.detach().requires_grad_(True)
-            Wx, dh = metropolis_aggregate(w.expand(-1, -1, Cx, -1, -1), xi, sh,
-                                          use_box=True, eps=1e-6)
+            # one weight channel read for all three image channels, the
+            # form the NKD_mp patch passes (its head mix keeps one channel)
+            Wx, dh = metropolis_aggregate(w, xi, sh, use_box=True, eps=1e-6)
             gwh, gx = torch.autograd.grad(Wx, (w, xi), gy)
             return Wx, gwh, gx
         return dict(inputs=[wh, x, gw], run=run, launches=2,

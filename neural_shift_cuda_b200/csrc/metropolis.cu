@@ -24,6 +24,9 @@
 
 #include <cmath>
 
+#include <cstdlib>
+
+#include "metropolis_tile.cuh"
 #include "nsc_common.cuh"
 #include "nsc_host.h"
 
@@ -338,6 +341,42 @@ nsc_status check_metro(const char* op, int64_t Cw, int64_t B, int64_t C,
     return build_shifts(op, shifts, S, 3, H, W, st);
 }
 
+// Geometry of the tiled kernels, or false when the call stays on the
+// one-pixel kernels (radius > 8, extents >= 2^30, or NSC_METRO_GENERIC).
+bool tile_geo(const ShiftTable& st, int64_t B, int64_t C, int64_t Cw, int64_t H,
+              int64_t W, mtile::Geo* g) {
+    if (getenv("NSC_METRO_GENERIC")) return false;
+    if (st.R > mtile::MAXR || H >= (1LL << 30) || W >= (1LL << 30) ||
+        B * Cw >= (1LL << 40))
+        return false;
+    g->B = static_cast<int>(B); g->C = static_cast<int>(C);
+    g->Cw = static_cast<int>(Cw); g->H = static_cast<int>(H);
+    g->W = static_cast<int>(W); g->S = st.S; g->R = st.R;
+    g->XP = mtile::TW + 2 * st.R;
+    g->XR = mtile::TH + 2 * st.R;
+    g->tiles_x = static_cast<int>((W + mtile::TW - 1) / mtile::TW);
+    g->ntiles = static_cast<int64_t>(g->tiles_x) * ((H + mtile::TH - 1) / mtile::TH);
+    g->groups = B * Cw;
+    return true;
+}
+
+inline dim3 tile_grid(const mtile::Geo& g) {
+    return dim3(static_cast<unsigned>(g.ntiles < (1LL << 31) - 1 ? g.ntiles : (1LL << 31) - 1),
+                static_cast<unsigned>(g.groups < 65535 ? g.groups : 65535));
+}
+
+// Dynamic shared memory of a tiled kernel with `planes` staged planes.
+template <typename K>
+bool tile_smem(K kern, const mtile::Geo& g, int planes, size_t elem, size_t* bytes) {
+    *bytes = static_cast<size_t>(planes) * g.XR * g.XP * elem;
+    if (*bytes > 200 * 1024) return false;
+    if (*bytes > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(*bytes)) != cudaSuccess)
+        return false;
+    return true;
+}
+
 }  // namespace
 }  // namespace nsc
 
@@ -361,6 +400,26 @@ nsc_status nsc_metropolis_fwd(const void* w_half, int w_dtype, int64_t w_channel
         using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
         using A = typename Acc<T>::type;
         const int64_t groups = B * w_channels;
+        mtile::Geo tg;
+        if (tile_geo(st, B, C, w_channels, H, W, &tg)) {
+            bool launched = false;
+            with_nc(C, w_channels, [&](auto tag) {
+                constexpr int NC = decltype(tag)::value_nc;
+                auto agg = mtile::aggregate_tile<T, NC>;
+                size_t smem = 0;
+                if (!tile_smem(agg, tg, 1 + NC, sizeof(A), &smem)) return;
+                mtile::degree_tile<T><<<tile_grid(tg), dim3(mtile::TX, mtile::TY), 0, sm>>>(
+                    static_cast<const T*>(w_half), static_cast<A*>(degree), st, tg,
+                    use_box ? 1 : 0);
+                agg<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), smem, sm>>>(
+                    static_cast<const T*>(w_half), static_cast<const T*>(img),
+                    static_cast<const A*>(degree), static_cast<T*>(Wx),
+                    static_cast<T*>(d_hat), st, tg, use_box ? 1 : 0,
+                    static_cast<A>(eps));
+                launched = true;
+            });
+            if (launched) return check_launch(op);
+        }
         metro_degree_kernel<T><<<grid_for(W, H, groups), dim3(kBX, kBY), 0, sm>>>(
             static_cast<const T*>(w_half), static_cast<A*>(degree), st, B,
             w_channels, H, W, use_box ? 1 : 0, groups);
@@ -399,6 +458,32 @@ nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype, int64_t w_channel
         using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
         using A = typename Acc<T>::type;
         const int64_t groups = B * w_channels;
+        mtile::Geo tg;
+        if (tile_geo(st, B, C, w_channels, H, W, &tg)) {
+            bool launched = false;
+            with_nc(C, w_channels, [&](auto tag) {
+                constexpr int NC = decltype(tag)::value_nc;
+                auto ka = mtile::bwd_a_tile<T, NC>;
+                auto kb = mtile::bwd_b_tile<T, NC>;
+                size_t sa = 0, sb = 0;
+                if (!tile_smem(ka, tg, 3 + 2 * NC, sizeof(A), &sa) ||
+                    !tile_smem(kb, tg, 4 + 2 * NC, sizeof(A), &sb))
+                    return;
+                ka<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sa, sm>>>(
+                    static_cast<const T*>(w_half), static_cast<const T*>(img),
+                    static_cast<const A*>(degree), static_cast<const T*>(d_hat),
+                    static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),
+                    static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st, tg,
+                    use_box ? 1 : 0, static_cast<A>(eps));
+                kb<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sb, sm>>>(
+                    static_cast<const T*>(img), static_cast<const A*>(degree),
+                    static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),
+                    static_cast<const A*>(grad_degree), static_cast<T*>(grad_w), st,
+                    tg, use_box ? 1 : 0, static_cast<A>(eps));
+                launched = true;
+            });
+            if (launched) return check_launch(op);
+        }
         with_nc(C, w_channels, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             metro_bwd_a_kernel<T, NC><<<grid_for(W, H, groups), dim3(kBX, kBY),

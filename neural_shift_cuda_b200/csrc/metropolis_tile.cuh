@@ -1,0 +1,504 @@
+// metropolis_tile.cuh -- tiled forms of the four Metropolis kernels
+// (degree, aggregation, backward passes A and B) for shift tables of radius
+// R <= 8.  The quantities are those of the one-pixel kernels of
+// metropolis.cu (see the formulas there); what changes is where operands
+// come from and how the denominators are formed.
+//
+// A CTA (32 x 8 threads, two pixels per thread) owns a 16 x 32 tile of one
+// (image, weight channel) group.  Every per-pixel quantity an edge reads at
+// a neighbour is staged once, with a circular R-pixel halo, in shared
+// memory in the accumulator type; an edge reads its neighbour at the
+// constant offset dx * pitch + dy.  Staged planes:
+//   r(p) = 1 / max(d(p), eps)      (so 1 / den_e(p) = min(r(p), r(p + delta)):
+//                                   max and round-to-nearest are monotonic,
+//                                   hence exact; one division per staged
+//                                   pixel instead of one per edge)
+//   d(p), image channels, grad_Wx, and the per-pixel backward term
+//   a(p) = sum_c gdh(p, c) - gWx(p, c) x(p, c).
+// Weight planes are read straight from global memory: w_s(q) coalesced
+// along the row, the mirror weight w_s(q - d) one row and column away
+// (L1/L2).  Tiles whose R-halo lies inside the image take a branch-free
+// form: no box masks and no wrapped addresses.  In-plane indexing is
+// 32-bit.
+#pragma once
+
+#include <cstdint>
+
+#include "nsc_common.cuh"
+
+namespace nsc {
+namespace mtile {
+
+constexpr int TX = 32, TY = 8, PPT = 2;
+constexpr int TH = TY * PPT, TW = TX;
+constexpr int NT = TX * TY;
+constexpr int MAXR = 8;
+
+struct Geo {
+    int B, C, Cw, H, W, S, R;
+    int XP, XR;                 // halo tile pitch and rows
+    int tiles_x;
+    int64_t ntiles, groups;
+};
+
+__device__ __forceinline__ int pmod(int a, int n) {
+    const int r = a % n;
+    return r < 0 ? r + n : r;
+}
+__device__ __forceinline__ int wrapc(int i, int n) {   // |i - [0,n)| <= n
+    return i < 0 ? i + n : (i >= n ? i - n : i);
+}
+
+// Visits every element (idx, global offset) of the halo tile.
+template <typename F>
+__device__ __forceinline__ void for_halo(const Geo& g, int h0, int w0, F&& f) {
+    const int tid = threadIdx.y * TX + threadIdx.x;
+    for (int idx = tid; idx < g.XR * g.XP; idx += NT) {
+        const int i = idx / g.XP;
+        const int j = idx - i * g.XP;
+        const int r = pmod(h0 - g.R + i, g.H);
+        const int c = pmod(w0 - g.R + j, g.W);
+        f(idx, static_cast<int64_t>(r) * g.W + c);
+    }
+}
+
+template <typename A>
+__device__ __forceinline__ A share_of(A self, A other) {
+    return self > other ? A(1) : (self == other ? A(0.5) : A(0));
+}
+__device__ __forceinline__ float amin(float a, float b) { return fminf(a, b); }
+__device__ __forceinline__ double amin(double a, double b) { return fmin(a, b); }
+
+struct Where {
+    int b, wc, c0, h0, w0;
+    bool interior;   // tile + R halo inside the image
+};
+__device__ __forceinline__ Where where(const Geo& g, int64_t tile, int64_t grp) {
+    Where o;
+    o.b = static_cast<int>(grp / g.Cw);
+    o.wc = static_cast<int>(grp - static_cast<int64_t>(o.b) * g.Cw);
+    o.c0 = (g.Cw == 1) ? 0 : o.wc;
+    const int ty = static_cast<int>(tile / g.tiles_x);
+    o.h0 = ty * TH;
+    o.w0 = static_cast<int>(tile - static_cast<int64_t>(ty) * g.tiles_x) * TW;
+    o.interior = o.h0 - g.R >= 0 && o.h0 + TH + g.R <= g.H && o.w0 - g.R >= 0 &&
+                 o.w0 + TW + g.R <= g.W;
+    return o;
+}
+
+// Per-shift weight addresses of one pixel: own w_s(q) and mirror w_s(q - d)
+// offsets inside the (b, s, wc) plane, and the box flags.
+struct EdgeGeom {
+    int64_t q, m;
+    bool in_p, in_m;
+};
+template <bool BORDER>
+__device__ __forceinline__ EdgeGeom edge_geom(const Geo& g, int h, int w, int dx, int dy) {
+    EdgeGeom e;
+    e.q = static_cast<int64_t>(h) * g.W + w;
+    if constexpr (BORDER) {
+        e.m = static_cast<int64_t>(wrapc(h - dx, g.H)) * g.W + wrapc(w - dy, g.W);
+        e.in_p = static_cast<unsigned>(h + dx) < static_cast<unsigned>(g.H) &&
+                 static_cast<unsigned>(w + dy) < static_cast<unsigned>(g.W);
+        e.in_m = static_cast<unsigned>(h - dx) < static_cast<unsigned>(g.H) &&
+                 static_cast<unsigned>(w - dy) < static_cast<unsigned>(g.W);
+    } else {
+        e.m = e.q - (static_cast<int64_t>(dx) * g.W + dy);
+        e.in_p = e.in_m = true;
+    }
+    return e;
+}
+
+// ---------------------------------------------------------------- degree
+template <typename T>
+__global__ void __launch_bounds__(NT)
+degree_tile(const T* __restrict__ w, typename Acc<T>::type* __restrict__ d,
+            const ShiftTable st, const Geo g, int use_box) {
+    using A = typename Acc<T>::type;
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            int hh[PPT];
+            A acc[PPT];
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                hh[p] = h < g.H ? h : g.H - 1;   // loads stay in bounds
+                acc[p] = A(0);
+            }
+            const T* wb = w + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 4
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const T* ws = wb + s * sstride;
+#pragma unroll
+                    for (int p = 0; p < PPT; ++p) {
+                        const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
+                        const A wq = ldg_acc<T, A>(ws + e.q);
+                        const A wm = ldg_acc<T, A>(ws + e.m);
+                        if (!use_box || e.in_p) acc[p] += wq;
+                        if (inv && (!use_box || e.in_m)) acc[p] += wm;
+                    }
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                if (h < g.H) d[grp * HW + static_cast<int64_t>(h) * g.W + wcol] = acc[p];
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------- aggregation
+template <typename T, int NC>
+__global__ void __launch_bounds__(NT)
+aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
+               const typename Acc<T>::type* __restrict__ d, T* __restrict__ Wx,
+               T* __restrict__ dhat, const ShiftTable st, const Geo g, int use_box,
+               typename Acc<T>::type eps) {
+    using A = typename Acc<T>::type;
+    extern __shared__ __align__(16) unsigned char smem_m[];
+    const int PL = g.XR * g.XP;
+    A* sr = reinterpret_cast<A*>(smem_m);     // 1 / max(d, eps)
+    A* sx = sr + PL;                          // [NC]
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
+            __syncthreads();
+            const A* dg = d + grp * HW;
+            for_halo(g, o.h0, o.w0, [&](int idx, int64_t off) {
+                const A dv = dg[off];
+                sr[idx] = A(1) / (dv > eps ? dv : eps);
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    sx[c * PL + idx] = static_cast<A>(to_acc(x[cb + c * HW + off]));
+            });
+            __syncthreads();
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            const T* wb = w + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            int hh[PPT], ci[PPT];
+            A ri[PPT], kx[PPT][NC], dh[PPT];
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                hh[p] = h < g.H ? h : g.H - 1;
+                ci[p] = (threadIdx.y + TY * p + g.R) * g.XP + threadIdx.x + g.R;
+                ri[p] = sr[ci[p]];
+                dh[p] = A(0);
+#pragma unroll
+                for (int c = 0; c < NC; ++c) kx[p][c] = A(0);
+            }
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 2
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const int off = dx * g.XP + dy;
+                    const T* ws = wb + s * sstride;
+#pragma unroll
+                    for (int p = 0; p < PPT; ++p) {
+                        const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
+                        const A wq = ldg_acc<T, A>(ws + e.q);
+                        const A wm = ldg_acc<T, A>(ws + e.m);
+                        if (!use_box || e.in_p) {
+                            const int n = ci[p] + off;
+                            const A wk = wq * amin(ri[p], sr[n]);
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) kx[p][c] += wk * sx[c * PL + n];
+                            dh[p] += wk;
+                        }
+                        if (inv && (!use_box || e.in_m)) {
+                            const int n = ci[p] - off;
+                            const A wk = wm * amin(ri[p], sr[n]);
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) kx[p][c] += wk * sx[c * PL + n];
+                            dh[p] += wk;
+                        }
+                    }
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                if (h >= g.H) continue;
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int64_t oi = cb + c * HW + static_cast<int64_t>(h) * g.W + wcol;
+                    const A xv = sx[c * PL + ci[p]];
+                    const A dhx = dh[p] * xv;
+                    Wx[oi] = static_cast<T>((xv - dhx) + kx[p][c]);
+                    dhat[oi] = static_cast<T>(dh[p]);
+                }
+            }
+        }
+    }
+}
+
+// Stages d, r = 1/max(d, eps), image channels, grad_Wx and the per-pixel
+// backward term a(p) = sum_c gdh - gWx x (in channel order).
+template <typename T, int NC, typename A>
+__device__ __forceinline__ void stage_bwd(const Geo& g, const Where& o, int64_t grp,
+                                          int64_t cb, int64_t HW, const A* __restrict__ d,
+                                          const T* __restrict__ x, const T* __restrict__ gWx,
+                                          const T* __restrict__ gdh, A eps, A* sd, A* sr,
+                                          A* sa, A* sx, A* sg) {
+    const int PL = g.XR * g.XP;
+    const A* dg = d + grp * HW;
+    for_halo(g, o.h0, o.w0, [&](int idx, int64_t off) {
+        const A dv = dg[off];
+        sd[idx] = dv;
+        sr[idx] = A(1) / (dv > eps ? dv : eps);
+        A a = A(0);
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const A xv = static_cast<A>(to_acc(x[cb + c * HW + off]));
+            const A gv = static_cast<A>(to_acc(gWx[cb + c * HW + off]));
+            sx[c * PL + idx] = xv;
+            sg[c * PL + idx] = gv;
+            a += static_cast<A>(to_acc(gdh[cb + c * HW + off])) - gv * xv;
+        }
+        sa[idx] = a;
+    });
+}
+
+// ------------------------------------------------------------ backward A
+// grad_img and the degree gradient g_d.  Per edge touching q:
+//   own edge e at q (neighbour n = q + delta):
+//     G = a(q) + sum_c gWx(q) x(n);  g_d(q) -= G wt r^2 share(d(q), d(n))
+//   edge of p = q - delta whose neighbour is q (weight wt_p, wk = wt_p r):
+//     G = a(p) + sum_c gWx(p) x(q);  g_d(q) -= G wt_p r^2 share(d(q), d(p))
+//     gx(q) += gWx(p) wk
+// with r = min(r(q), r(other)); g_d terms only where max(d(q), d(other))
+// >= eps (clamp_min passes no gradient below eps).  The terms come in pairs
+// over one pixel pair {q, n}: same weight, denominator and tie share (the
+// own forward edge of q with the mirror edge of q + d, the forward edge of
+// q - d with the own mirror edge of q), so each pair is evaluated once.
+template <typename T, int NC>
+__global__ void __launch_bounds__(NT)
+bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
+           const typename Acc<T>::type* __restrict__ d, const T* __restrict__ dhat,
+           const T* __restrict__ gWx, const T* __restrict__ gdh,
+           typename Acc<T>::type* __restrict__ gd, T* __restrict__ gx,
+           const ShiftTable st, const Geo g, int use_box, typename Acc<T>::type eps) {
+    using A = typename Acc<T>::type;
+    extern __shared__ __align__(16) unsigned char smem_m[];
+    const int PL = g.XR * g.XP;
+    A* sd = reinterpret_cast<A*>(smem_m);
+    A* sr = sd + PL;
+    A* sa = sr + PL;
+    A* sx = sa + PL;                // [NC]
+    A* sg = sx + NC * PL;           // [NC]
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
+            __syncthreads();
+            stage_bwd<T, NC>(g, o, grp, cb, HW, d, x, gWx, gdh, eps, sd, sr, sa, sx, sg);
+            __syncthreads();
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            const T* wb = w + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            int hh[PPT], ci[PPT];
+            A di[PPT], ri[PPT], aq[PPT], xq[PPT][NC], gq[PPT][NC], gxa[PPT][NC], g_d[PPT];
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                hh[p] = h < g.H ? h : g.H - 1;
+                ci[p] = (threadIdx.y + TY * p + g.R) * g.XP + threadIdx.x + g.R;
+                di[p] = sd[ci[p]];
+                ri[p] = sr[ci[p]];
+                aq[p] = sa[ci[p]];
+                g_d[p] = A(0);
+                const int64_t q = static_cast<int64_t>(hh[p]) * g.W + wcol;
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    xq[p][c] = sx[c * PL + ci[p]];
+                    gq[p][c] = sg[c * PL + ci[p]];
+                    gxa[p][c] = gq[p][c] * (A(1) - static_cast<A>(to_acc(dhat[cb + c * HW + q])));
+                }
+            }
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 1
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const int off = dx * g.XP + dy;
+                    const T* ws = wb + s * sstride;
+#pragma unroll
+                    for (int p = 0; p < PPT; ++p) {
+                        const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
+                        const A w_q = ldg_acc<T, A>(ws + e.q);
+                        const A w_m = ldg_acc<T, A>(ws + e.m);
+                        const bool kp = !use_box || e.in_p, km = !use_box || e.in_m;
+                        // Pair (q, q + d), weight w_s(q): own forward edge of q
+                        // and (inv) the mirror edge of q + d ending at q.
+                        if (kp && w_q != A(0)) {
+                            const int n = ci[p] + off;
+                            const A dn = sd[n];
+                            const A r = amin(ri[p], sr[n]);
+                            A Tq = aq[p], Tn = A(0);
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) Tq += gq[p][c] * sx[c * PL + n];
+                            if (inv) {
+                                const A wk = w_q * r;
+                                Tn = sa[n];
+#pragma unroll
+                                for (int c = 0; c < NC; ++c) {
+                                    const A gn = sg[c * PL + n];
+                                    Tn += gn * xq[p][c];
+                                    gxa[p][c] += gn * wk;
+                                }
+                            }
+                            if ((di[p] > dn ? di[p] : dn) >= eps)
+                                g_d[p] -= (Tq + Tn) * w_q * r * r * share_of(di[p], dn);
+                        }
+                        // Pair (q, q - d), weight w_s(q - d): forward edge of
+                        // q - d ending at q and (inv) the own mirror edge of q.
+                        if (km && w_m != A(0)) {
+                            const int n = ci[p] - off;
+                            const A dn = sd[n];
+                            const A r = amin(ri[p], sr[n]);
+                            const A wk = w_m * r;
+                            A Tn = sa[n], Tq = A(0);
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) {
+                                const A gn = sg[c * PL + n];
+                                Tn += gn * xq[p][c];
+                                gxa[p][c] += gn * wk;
+                            }
+                            if (inv) {
+                                Tq = aq[p];
+#pragma unroll
+                                for (int c = 0; c < NC; ++c) Tq += gq[p][c] * sx[c * PL + n];
+                            }
+                            if ((di[p] > dn ? di[p] : dn) >= eps)
+                                g_d[p] -= (Tn + Tq) * w_m * r * r * share_of(di[p], dn);
+                        }
+                    }
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                if (h >= g.H) continue;
+                const int64_t q = static_cast<int64_t>(h) * g.W + wcol;
+                gd[grp * HW + q] = g_d[p];
+#pragma unroll
+                for (int c = 0; c < NC; ++c) gx[cb + c * HW + q] = static_cast<T>(gxa[p][c]);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------ backward B
+// grad_w without reading w:
+//   gw_s(q) = keep_f(q) (G_f r + g_d(q)) + inv keep_i(q + d) (G_m r + g_d(q + d))
+//   G_f = a(q) + sum_c gWx(q) x(q + d),  G_m = a(q + d) + sum_c gWx(q + d) x(q)
+// with r = min(r(q), r(q + d)); keep_i(q + d) = [q + d inside] = keep_f(q).
+template <typename T, int NC>
+__global__ void __launch_bounds__(NT)
+bwd_b_tile(const T* __restrict__ x, const typename Acc<T>::type* __restrict__ d,
+           const T* __restrict__ gWx, const T* __restrict__ gdh,
+           const typename Acc<T>::type* __restrict__ gd, T* __restrict__ gw,
+           const ShiftTable st, const Geo g, int use_box, typename Acc<T>::type eps) {
+    using A = typename Acc<T>::type;
+    extern __shared__ __align__(16) unsigned char smem_m[];
+    const int PL = g.XR * g.XP;
+    A* sd = reinterpret_cast<A*>(smem_m);
+    A* sr = sd + PL;
+    A* sa = sr + PL;
+    A* sgd = sa + PL;
+    A* sx = sgd + PL;               // [NC]
+    A* sg = sx + NC * PL;           // [NC]
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
+            __syncthreads();
+            stage_bwd<T, NC>(g, o, grp, cb, HW, d, x, gWx, gdh, eps, sd, sr, sa, sx, sg);
+            const A* gdg = gd + grp * HW;
+            for_halo(g, o.h0, o.w0, [&](int idx, int64_t off) { sgd[idx] = gdg[off]; });
+            __syncthreads();
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            T* gwb = gw + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            int hh[PPT], ci[PPT];
+            bool act[PPT];
+            A ri[PPT], gdi[PPT], aq[PPT], xq[PPT][NC], gq[PPT][NC];
+#pragma unroll
+            for (int p = 0; p < PPT; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                act[p] = h < g.H;
+                hh[p] = act[p] ? h : g.H - 1;
+                ci[p] = (threadIdx.y + TY * p + g.R) * g.XP + threadIdx.x + g.R;
+                ri[p] = sr[ci[p]];
+                gdi[p] = sgd[ci[p]];
+                aq[p] = sa[ci[p]];
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    xq[p][c] = sx[c * PL + ci[p]];
+                    gq[p][c] = sg[c * PL + ci[p]];
+                }
+            }
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 2
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const int off = dx * g.XP + dy;
+                    T* gws = gwb + s * sstride;
+#pragma unroll
+                    for (int p = 0; p < PPT; ++p) {
+                        const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
+                        const int qp = ci[p] + off;
+                        const A r = amin(ri[p], sr[qp]);
+                        A v = A(0);
+                        if (!use_box || e.in_p) {
+                            A G = aq[p];
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) G += gq[p][c] * sx[c * PL + qp];
+                            v += G * r + gdi[p];
+                            if (inv) {
+                                A Gm = sa[qp];
+#pragma unroll
+                                for (int c = 0; c < NC; ++c) Gm += sg[c * PL + qp] * xq[p][c];
+                                v += Gm * r + sgd[qp];
+                            }
+                        }
+                        if (act[p]) gws[e.q] = static_cast<T>(v);
+                    }
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
+        }
+    }
+}
+
+}  // namespace mtile
+}  // namespace nsc

@@ -56,7 +56,8 @@ bool norm_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     if (H >= (1LL << 30) || W >= (1LL << 30) || B * C >= (1LL << 30))
         NDECLINE("extent too large for the tiled path");
     const int es = xd == NSC_F32 ? 4 : 2;
-    const int V = 16 / es;
+    const int V = KB / es;
+    const int VX = 16 / es;
     if ((W * es) % 16 || reinterpret_cast<uintptr_t>(x) % 16 ||
         reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(D) % 16 ||
         reinterpret_cast<uintptr_t>(L) % 16)
@@ -103,7 +104,7 @@ bool norm_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     g.tiles_y = static_cast<int>((H + TH - 1) / TH);
     g.Rx = Rx;
     g.XH = TH + 2 * Rx;
-    const int XC = (K + V - 1) / V * V;
+    const int XC = (K + VX - 1) / VX * VX;
     g.XW = TW + 2 * XC;
     g.groups = B * ((Cw == 1) ? 1 : C);
     g.step_stride = B * Cw * H * W;

@@ -39,8 +39,14 @@
 namespace nsc {
 namespace nfast {
 
-constexpr int TPR = 16;             // threads per row
-constexpr int TH = 16;              // rows per tile
+// Key bytes per thread and shift: 16 (8 fp16/bf16 pixels) or 8 (4 pixels,
+// half the unrolled code and registers, so more CTAs per SM).
+#ifndef NSC_NORM_KB
+#define NSC_NORM_KB 8
+#endif
+constexpr int KB = NSC_NORM_KB;
+constexpr int TPR = 256 / KB;       // threads per row: 128 bytes of keys
+constexpr int TH = 256 / TPR;       // rows per tile
 constexpr int NT = TPR * TH;        // 256 threads
 constexpr int NST = 8;              // key ring slots per thread
 constexpr int MAXR = 16;            // |dx|, |dy| <= MAXR on this path
@@ -74,6 +80,14 @@ __device__ __forceinline__ void cp_async16_n(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src)
                  : "memory");
 }
+__device__ __forceinline__ void cp_async_kb(uint32_t dst, const void* src) {
+    if constexpr (KB == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src)
+                     : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src)
+                     : "memory");
+}
 __device__ __forceinline__ void cp_async_commit_n() {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -87,25 +101,25 @@ __device__ __forceinline__ uint4 lds128v(uint32_t a) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
-// Words [K, HI) of the shared-memory row at byte address `a` (16-byte
-// aligned) into d[K - LO ...], with the widest aligned vector loads.
-template <int K, int HI, int LO, int N>
+// Words [K, HI) of the shared-memory row at byte address `a` (aligned to
+// 4*MAXW bytes) into d[K - LO ...], with the widest aligned vector loads.
+template <int K, int HI, int LO, int MAXW, int N>
 __device__ __forceinline__ void load_words(uint32_t (&d)[N], uint32_t a) {
     if constexpr (K < HI) {
-        if constexpr (K % 4 == 0 && K + 4 <= HI) {
+        if constexpr (MAXW >= 4 && K % 4 == 0 && K + 4 <= HI) {
             const uint4 v = lds128v(a + 4 * K);
             d[K - LO] = v.x; d[K - LO + 1] = v.y; d[K - LO + 2] = v.z; d[K - LO + 3] = v.w;
-            load_words<K + 4, HI, LO>(d, a);
+            load_words<K + 4, HI, LO, MAXW>(d, a);
         } else if constexpr (K % 2 == 0 && K + 2 <= HI) {
             uint32_t p, q;
             asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(p), "=r"(q) : "r"(a + 4 * K));
             d[K - LO] = p; d[K - LO + 1] = q;
-            load_words<K + 2, HI, LO>(d, a);
+            load_words<K + 2, HI, LO, MAXW>(d, a);
         } else {
             uint32_t p;
             asm volatile("ld.shared.u32 %0, [%1];" : "=r"(p) : "r"(a + 4 * K));
             d[K - LO] = p;
-            load_words<K + 1, HI, LO>(d, a);
+            load_words<K + 1, HI, LO, MAXW>(d, a);
         }
     }
 }
@@ -142,14 +156,15 @@ __device__ __forceinline__ int pmodi(int a, int n) {
 }
 
 template <typename T, int NC, int DYMIN, int DYMAX, bool LOGW>
-__global__ void __launch_bounds__(NT, 2)
+__global__ void __launch_bounds__(NT, KB == 16 ? 2 : 3)
 norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
                  float* __restrict__ D, float* __restrict__ L,
                  const NormTable tab, const NormGeo g, int* __restrict__ invalid) {
-    constexpr int V = 16 / static_cast<int>(sizeof(T));
+    constexpr int V = KB / static_cast<int>(sizeof(T));
     constexpr int EPW = 4 / static_cast<int>(sizeof(T));
     constexpr int TW = TPR * V;
-    constexpr int XC = ((DYMAX > -DYMIN ? DYMAX : -DYMIN) + V - 1) / V * V;
+    constexpr int VX = 16 / static_cast<int>(sizeof(T));   // staging chunk (16 bytes)
+    constexpr int XC = ((DYMAX > -DYMIN ? DYMAX : -DYMIN) + VX - 1) / VX * VX;
     constexpr int FLO = XC + DYMIN, FHI = XC + DYMAX + V;   // window, elements
     constexpr int FWL = FLO / EPW, FWH = (FHI + EPW - 1) / EPW;
     constexpr int NW = FWH - FWL;
@@ -157,14 +172,14 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
     static_assert(NDY <= 32, "dy mask is 32 bits");
 
     extern __shared__ __align__(16) unsigned char smem_n[];
-    uint4* ring = reinterpret_cast<uint4*>(smem_n);          // [NST][NT]
-    T* xs = reinterpret_cast<T*>(smem_n + NST * NT * 16);      // [NC][XH][XW]
+    unsigned char* ring = smem_n;                             // [NST][NT][KB]
+    T* xs = reinterpret_cast<T*>(smem_n + NST * NT * KB);      // [NC][XH][XW]
 
     const int tid = threadIdx.x;
     const int tr = tid / TPR, tc = tid % TPR;
     const int64_t HW = static_cast<int64_t>(g.H) * g.W;
     const int cgroups = (g.Cw == 1) ? (g.C + NC - 1) / NC : g.C;
-    const uint32_t ring32 = smem_addr(ring) + tid * 16u;
+    const uint32_t ring32 = smem_addr(ring) + tid * static_cast<uint32_t>(KB);
 
     for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
         const int b = static_cast<int>(grp / cgroups);
@@ -185,8 +200,8 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
                           static_cast<int64_t>(h) * g.W + wcol;
             auto issue = [&](int k) {
                 if (active && k < tab.nsteps)
-                    cp_async16_n(ring32 + (k % NST) * (NT * 16u),
-                                 wp + static_cast<int64_t>(tab.seq[k]) * g.step_stride);
+                    cp_async_kb(ring32 + (k % NST) * (NT * KB),
+                                wp + static_cast<int64_t>(tab.seq[k]) * g.step_stride);
                 cp_async_commit_n();
             };
             __syncthreads();   // previous tile's readers of xs are done
@@ -194,28 +209,28 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
             for (int k = 0; k < NST - 2; ++k) issue(k);
 
             // ---- x halo tile, circular rows and columns
-            const int nv = g.XW / V;
+            const int nv = g.XW / VX;
             const int xtotal = NC * g.XH * nv;
             for (int idx = tid; idx < xtotal; idx += NT) {
                 const int c = idx / (g.XH * nv);
                 const int rem = idx - c * g.XH * nv;
                 const int i = rem / nv;
                 const int jv = rem - i * nv;
-                T* dst = xs + (c * g.XH + i) * g.XW + jv * V;
+                T* dst = xs + (c * g.XH + i) * g.XW + jv * VX;
                 if (c >= nc) {
                     *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
                     continue;
                 }
                 const int r = pmodi(h0 - g.Rx + i, g.H);
-                const int col0 = w0 - XC + jv * V;
+                const int col0 = w0 - XC + jv * VX;
                 const T* src = x + (static_cast<int64_t>(b) * g.C + c0 + c) * HW +
                                static_cast<int64_t>(r) * g.W;
-                if (col0 >= 0 && col0 + V <= g.W) {
+                if (col0 >= 0 && col0 + VX <= g.W) {
                     *reinterpret_cast<uint4*>(dst) =
                         __ldg(reinterpret_cast<const uint4*>(src + col0));
                 } else {
 #pragma unroll
-                    for (int e = 0; e < V; ++e) dst[e] = src[pmodi(col0 + e, g.W)];
+                    for (int e = 0; e < VX; ++e) dst[e] = src[pmodi(col0 + e, g.W)];
                 }
             }
             __syncthreads();
@@ -236,7 +251,7 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
                 uint32_t xw[NC][NW];
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
-                    load_words<FWL, FWH, FWL>(xw[c], xs32 + static_cast<uint32_t>(
+                    load_words<FWL, FWH, FWL, KB / 4>(xw[c], xs32 + static_cast<uint32_t>(
                         ((c * g.XH + tr + dx + g.Rx) * g.XW) * sizeof(T)));
                 sfor<0, NDY>([&](auto jc) {
                     constexpr int j = decltype(jc)::value;
@@ -244,48 +259,77 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
                     if (!((pres >> j) & 1u)) return;
                     issue(k + NST - 2);
                     cp_async_wait_n<NST - 2>();
-                    const uint4 kv4 = lds128v(ring32 + (k % NST) * (NT * 16u));
-                    const uint32_t kw[4] = {kv4.x, kv4.y, kv4.z, kv4.w};
+                    uint32_t kw[KB / 4];
+                    if constexpr (KB == 16) {
+                        const uint4 kv4 = lds128v(ring32 + (k % NST) * (NT * KB));
+                        kw[0] = kv4.x; kw[1] = kv4.y; kw[2] = kv4.z; kw[3] = kv4.w;
+                    } else {
+                        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                                     : "=r"(kw[0]), "=r"(kw[1])
+                                     : "r"(ring32 + (k % NST) * (NT * KB)));
+                    }
                     ++k;
+                    // a_i before any rescale; one warp-uniform branch per
+                    // key vector moves the reference of the lanes/pixels
+                    // that need it (rare after the first keys).
+                    float a[V];
+                    float amax = -INFINITY, amin = INFINITY;
                     sfor<0, V>([&](auto ic) {
                         constexpr int i = decltype(ic)::value;
                         const float key = elem<T, i>(kw);
-                        float a;
                         if constexpr (LOGW) {
-                            float arg = fmaf(key, kLog2e, -mr[i]);
-                            if (arg > kLazy) {       // rare: move the reference
-                                const float mn = key * kLog2e;
-                                const float f = ex2_approx(mr[i] - mn);
-                                sz[i] *= f;
-#pragma unroll
-                                for (int c = 0; c < NC; ++c) su[c][i] *= f;
-                                mr[i] = mn;
-                                arg = fmaf(key, kLog2e, -mn);
-                            }
-                            a = ex2_approx(arg);
+                            a[i] = fmaf(key, kLog2e, -mr[i]);
                         } else {
-                            a = key * mr[i];
-                            if (!(a <= 65536.0f) || a < 0.f) {   // rare
-                                if (!(key >= 0.f) || key == INFINITY) {
-                                    sz[i] = __int_as_float(0x7fffffff);   // poison: NaN
-                                    a = 0.f;
-                                } else {
-                                    int e = ilogbf(key);
-                                    e = e < -100 ? -100 : (e > 126 ? 126 : e);
-                                    const float sc = __int_as_float((127 - e) << 23);
-                                    const float keep = mr[i] == INFINITY ? 0.f : sc / mr[i];
-                                    sz[i] *= keep;
+                            a[i] = key * mr[i];
+                            amin = fminf(amin, a[i]);
+                        }
+                        // NaN-propagating max: a NaN key takes the slow path
+                        asm("max.NaN.f32 %0, %0, %1;" : "+f"(amax) : "f"(a[i]));
+                    });
+                    const bool need = LOGW ? !(amax <= kLazy)
+                                           : (!(amax <= 65536.0f) || amin < 0.f);
+                    if (__builtin_expect(__any_sync(0xffffffffu, need), 0)) {
+                        sfor<0, V>([&](auto ic) {
+                            constexpr int i = decltype(ic)::value;
+                            const float key = elem<T, i>(kw);
+                            if constexpr (LOGW) {
+                                if (a[i] > kLazy) {
+                                    const float mn = key * kLog2e;
+                                    const float f = ex2_approx(mr[i] - mn);
+                                    sz[i] *= f;
 #pragma unroll
-                                    for (int c = 0; c < NC; ++c) su[c][i] *= keep;
-                                    mr[i] = sc;
-                                    a = key * sc;
+                                    for (int c = 0; c < NC; ++c) su[c][i] *= f;
+                                    mr[i] = mn;
+                                    a[i] = fmaf(key, kLog2e, -mn);
+                                }
+                            } else {
+                                if (!(a[i] <= 65536.0f) || a[i] < 0.f) {
+                                    if (!(key >= 0.f) || key == INFINITY) {
+                                        sz[i] = __int_as_float(0x7fffffff);   // poison: NaN
+                                        a[i] = 0.f;
+                                    } else {
+                                        // binary exponent (subnormals clamp below)
+                                        int e = static_cast<int>((__float_as_uint(key) >> 23) & 0xFFu) - 127;
+                                        e = e < -100 ? -100 : (e > 126 ? 126 : e);
+                                        const float sc = __int_as_float((127 - e) << 23);
+                                        const float keep = mr[i] == INFINITY ? 0.f : sc / mr[i];
+                                        sz[i] *= keep;
+#pragma unroll
+                                        for (int c = 0; c < NC; ++c) su[c][i] *= keep;
+                                        mr[i] = sc;
+                                        a[i] = key * sc;
+                                    }
                                 }
                             }
-                        }
-                        sz[i] += a;
+                        });
+                    }
+                    sfor<0, V>([&](auto ic) {
+                        constexpr int i = decltype(ic)::value;
+                        const float ai = LOGW ? ex2_approx(a[i]) : a[i];
+                        sz[i] += ai;
 #pragma unroll
                         for (int c = 0; c < NC; ++c)
-                            su[c][i] = fmaf(a, elem<T, XC + dy + i - FWL * EPW>(xw[c]), su[c][i]);
+                            su[c][i] = fmaf(ai, elem<T, XC + dy + i - FWL * EPW>(xw[c]), su[c][i]);
                     });
                 });
             }
@@ -309,7 +353,7 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
                         for (int c = 0; c < NC; ++c) d_out[c][i] = 0.f;
                     } else {
                         const float base = LOGW ? mr[i] * kLn2
-                                                : -static_cast<float>(ilogbf(mr[i])) * kLn2;
+                                                : -static_cast<float>(static_cast<int>((__float_as_uint(mr[i]) >> 23) & 0xFFu) - 127) * kLn2;
                         l_out[i] = base + logf(s);
 #pragma unroll
                         for (int c = 0; c < NC; ++c) d_out[c][i] = su[c][i] / s;
@@ -320,14 +364,19 @@ norm_fast_kernel(const T* __restrict__ x, const T* __restrict__ w,
                     if (c >= nc) continue;
                     const int64_t o = (static_cast<int64_t>(b) * g.C + c0 + c) * HW +
                                       static_cast<int64_t>(h) * g.W + wcol;
+                    if constexpr (V >= 4) {
 #pragma unroll
-                    for (int q = 0; q < V / 4; ++q) {
-                        *reinterpret_cast<float4*>(D + o + 4 * q) =
-                            make_float4(d_out[c][4 * q], d_out[c][4 * q + 1],
-                                        d_out[c][4 * q + 2], d_out[c][4 * q + 3]);
-                        *reinterpret_cast<float4*>(L + o + 4 * q) =
-                            make_float4(l_out[4 * q], l_out[4 * q + 1],
-                                        l_out[4 * q + 2], l_out[4 * q + 3]);
+                        for (int q = 0; q < V / 4; ++q) {
+                            *reinterpret_cast<float4*>(D + o + 4 * q) =
+                                make_float4(d_out[c][4 * q], d_out[c][4 * q + 1],
+                                            d_out[c][4 * q + 2], d_out[c][4 * q + 3]);
+                            *reinterpret_cast<float4*>(L + o + 4 * q) =
+                                make_float4(l_out[4 * q], l_out[4 * q + 1],
+                                            l_out[4 * q + 2], l_out[4 * q + 3]);
+                        }
+                    } else {
+                        *reinterpret_cast<float2*>(D + o) = make_float2(d_out[c][0], d_out[c][1]);
+                        *reinterpret_cast<float2*>(L + o) = make_float2(l_out[0], l_out[1]);
                     }
                 }
                 if (bad && invalid) atomicOr(invalid, 1);

@@ -10,15 +10,13 @@ namespace nfast {
 template <typename T, int NC, int DYMIN, int DYMAX, bool LOGW>
 bool launch(const void* x, const void* w, void* D, void* L, const NormTable& tab,
             const NormGeo& g, int* invalid, cudaStream_t stream) {
-    constexpr int V = 16 / static_cast<int>(sizeof(T));
-    const size_t smem = static_cast<size_t>(NST) * NT * 16 +
+    const size_t smem = static_cast<size_t>(NST) * NT * KB +
                         static_cast<size_t>(NC) * g.XH * g.XW * sizeof(T);
     auto kern = norm_fast_kernel<T, NC, DYMIN, DYMAX, LOGW>;
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return false;
-    (void)V;
     const int64_t ntiles = static_cast<int64_t>(g.tiles_x) * g.tiles_y;
     const unsigned gx = static_cast<unsigned>(ntiles < (1LL << 31) - 1 ? ntiles : (1LL << 31) - 1);
     const unsigned gy = static_cast<unsigned>(g.groups < 65535 ? g.groups : 65535);

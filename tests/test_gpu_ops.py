@@ -421,9 +421,13 @@ def test_metropolis_golden(cuda, name):
     close(xc.grad, c["gx"], 1e-9, 1e-10)
 
 
+@pytest.mark.parametrize("generic", [False, True])
 @pytest.mark.parametrize("use_box", [True, False])
 @pytest.mark.parametrize("bcast", [False, True])
-def test_metropolis_vs_oracle(cuda, use_box, bcast):
+def test_metropolis_vs_oracle(cuda, use_box, bcast, generic, monkeypatch):
+    """Both kernel families (halo-tiled, one pixel per thread) in fp64."""
+    if generic:
+        monkeypatch.setenv("NSC_METRO_GENERIC", "1")
     torch.manual_seed(11)
     B, C, H, W, R = 2, 3, 17, 19, 2
     rows = O.halfplane_shifts(R)
@@ -455,3 +459,31 @@ def test_metropolis_fp32(cuda):
                                     x.double(), rows, True)
     close(Wx, Wr.float(), 1e-5, 1e-5)
     close(dh, dr.float(), 1e-5, 1e-5)
+
+
+def _metro_run(w, x, rows, use_box, gW, gd):
+    wc = w.cuda().requires_grad_(True)
+    xc = x.cuda().requires_grad_(True)
+    Wx, dh = nsc.metropolis_aggregate(wc, xc, rows, use_box)
+    (Wx * gW.cuda() + dh * gd.cuda()).sum().backward()
+    return [t.detach().cpu() for t in (Wx, dh, wc.grad, xc.grad)]
+
+
+@pytest.mark.parametrize("R,H,W,bcast,use_box", [
+    (5, 37, 45, True, True), (5, 16, 32, False, False), (8, 20, 70, True, False),
+    (1, 5, 3, True, True),
+])
+def test_metropolis_tiled_matches_general(cuda, R, H, W, bcast, use_box, monkeypatch):
+    """fp32: the tiled kernels do the general kernels' arithmetic in the
+    same order, so forward and gradients agree to rounding of contraction."""
+    torch.manual_seed(R + H)
+    rows = O.halfplane_shifts(R)
+    B, C = 2, 3
+    w = torch.sigmoid(torch.randn(B, len(rows), 1 if bcast else C, H, W))
+    x = torch.rand(B, C, H, W)
+    gW, gd = torch.randn_like(x), torch.randn_like(x)
+    tiled = _metro_run(w, x, rows, use_box, gW, gd)
+    monkeypatch.setenv("NSC_METRO_GENERIC", "1")
+    general = _metro_run(w, x, rows, use_box, gW, gd)
+    for a, b in zip(tiled, general):
+        torch.testing.assert_close(a, b, rtol=2e-6, atol=2e-6)
