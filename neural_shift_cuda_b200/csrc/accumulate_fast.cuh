@@ -606,16 +606,12 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             const uint64_t m_pres = tab.present[dx + MAXR], m_inv = tab.inv[dx + MAXR];
             const uint64_t m_first = tab.first[dx + MAXR], m_second = tab.second[dx + MAXR];
             uint32_t stp = stages32 + stage * g.stage_stride;
-            uint32_t stp2 = stp + g.plane_bytes;
             auto one = [&](auto dyc, const bool second, const bool first, const bool inv) {
                 constexpr int dy = decltype(dyc)::value;
-                if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && !second && !dead) {
-                    if (!mbar_wait32(full32 + 8 * stage, phase, timeouts)) {
-                        dead = true;
-                        *(volatile int*)&abort_flag = 1;
-                    }
-                }
-                const uint32_t sp = after(second ? stp2 : stp);
+                if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && !second)
+                    mbar_wait32_ab(full32 + 8 * stage, phase, timeouts,
+                                   (volatile int*)&abort_flag);
+                const uint32_t sp = after(second ? stp + g.plane_bytes : stp);
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
                 lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
@@ -656,7 +652,6 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                     } else {
                         stp += g.stage_stride;
                     }
-                    stp2 = stp + g.plane_bytes;
                 }
             };
             if constexpr (EXACT) {

@@ -101,6 +101,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     atomicAdd(timeouts, 1u);
     return false;
 }
+// As mbar_wait32, but a CTA-wide abort flag (shared memory) is checked
+// before any suspension: once one thread gave up, the others return at once
+// instead of each running out its own limit.  The fast path (phase already
+// complete) is a single try_wait.
+static __device__ __noinline__ bool mbar_wait32_slow(uint32_t bar, uint32_t parity,
+                                              unsigned int* timeouts,
+                                              volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    for (uint32_t i = 0; i < kSleepWaits; ++i) {
+        if (mbar_try_wait_sleep32(bar, parity)) return true;
+        if ((i & 63u) == 63u && *abort_flag) return false;
+    }
+    atomicAdd(timeouts, 1u);
+    *abort_flag = 1;
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait32_ab(uint32_t bar, uint32_t parity,
+                                               unsigned int* timeouts,
+                                               volatile int* abort_flag) {
+    if (mbar_try_wait32(bar, parity)) return true;
+    return mbar_wait32_slow(bar, parity, timeouts, abort_flag);
+}
 __device__ __forceinline__ bool mbar_wait32(uint32_t bar, uint32_t parity,
                                             unsigned int* timeouts) {
     if (mbar_try_wait32(bar, parity)) return true;
