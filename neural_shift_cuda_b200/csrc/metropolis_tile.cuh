@@ -29,7 +29,10 @@
 namespace nsc {
 namespace mtile {
 
-constexpr int TX = 32, TY = 8, PPT = 2;
+#ifndef NSC_METRO_PPT
+#define NSC_METRO_PPT 2
+#endif
+constexpr int TX = 32, TY = 8, PPT = NSC_METRO_PPT;   // pixels per thread (rows TY apart)
 constexpr int TH = TY * PPT, TW = TX;
 constexpr int NT = TX * TY;
 constexpr int MAXR = 8;
