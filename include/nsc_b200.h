@@ -143,7 +143,7 @@ NSC_API nsc_status nsc_accumulate_uz_band_fwd(const void* x_ext, int x_dtype,
 /* Mirror contributions of this band's own weights to the R rows just
  * above (edge_top: global rows row0-R .. row0-1) and just below
  * (edge_bot: rows row0+Hb .. row0+Hb+R-1) the band.  edge_top / edge_bot
- * are (2, B, C, R, W) accumulators (U part then Z part, fp32/fp64),
+ * are (2, B, C, R, W) accumulators (U part then Z part, fp32/fp64; R <= 32),
  * overwritten.  Rows outside the image [0, Hg) receive zeros. */
 NSC_API nsc_status nsc_accumulate_uz_band_edges(const void* x_ext, int x_dtype,
                                         const void* w, int w_dtype,
@@ -153,6 +153,18 @@ NSC_API nsc_status nsc_accumulate_uz_band_edges(const void* x_ext, int x_dtype,
                                         const int64_t* shifts, int64_t S,
                                         void* edge_top, void* edge_bot,
                                         void* stream);
+
+/* Adds the neighbours' mirror strips to a band's (U, Z) in one launch:
+ * strip_above (the upper band's edge_bot, may be NULL) onto rows 0 .. R-1,
+ * strip_below (the lower band's edge_top, may be NULL) onto rows
+ * Hb-R .. Hb-1.  acc_dtype: NSC_F32 or NSC_F64 (the type of U, Z and the
+ * strips).  No reference counterpart (part of the row-band split). */
+NSC_API nsc_status nsc_accumulate_uz_band_add_strips(void* U, void* Z, int acc_dtype,
+                                             int64_t B, int64_t C, int64_t Hb,
+                                             int64_t W, int64_t R,
+                                             const void* strip_above,
+                                             const void* strip_below,
+                                             void* stream);
 
 /* ---------------------------------------------------------------------
  * normalized_accumulate_uz.  Replaces normalized_accumulate_uz_forward /

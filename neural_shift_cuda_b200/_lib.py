@@ -53,6 +53,8 @@ _SIGS = {
                                    _L, _LP, _L, _P, _P, _P],
     "nsc_accumulate_uz_band_edges": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _L,
                                      _L, _LP, _L, _P, _P, _P],
+    "nsc_accumulate_uz_band_add_strips": [_P, _P, _I, _L, _L, _L, _L, _L, _P,
+                                          _P, _P],
     "nsc_normalized_accumulate_uz_fwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L,
                                          _LP, _L, _I, _P, _P, _P, _P],
     "nsc_normalized_accumulate_uz_bwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L,

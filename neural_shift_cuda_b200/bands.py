@@ -18,9 +18,13 @@ identical to the unsplit op:
    owns those rows, which adds them.  The mirror term is never periodic, so
    the strips of the first and last band are not exchanged.
 
-Both exchanges are one grouped send/recv step each (`batch_isend_irecv`,
-NCCL over NVLink for CUDA tensors).  The compute is injectable so the
-exchange logic runs on CPU `gloo` ranks in the tests.
+The strips need only the rank's own rows, so they are computed first and
+both exchanges travel in ONE grouped send/recv (`batch_isend_irecv`, NCCL
+over NVLink for CUDA tensors) before the band forward.  With
+`padded=True` the caller's x buffer has R spare rows above and below the
+band and the halo is received straight into them (no band-sized copy per
+step).  The compute is injectable so the exchange logic runs on CPU `gloo`
+ranks in the tests.
 """
 
 from __future__ import annotations
@@ -33,6 +37,7 @@ from . import _lib
 from .ops import _require_cuda, _storage_dtypes
 
 __all__ = ["band_rows", "x_ext_from_full", "band_compute_cuda",
+           "band_forward_cuda", "band_edges_cuda",
            "accumulate_uz_banded_local", "accumulate_uz_banded",
            "radius_of"]
 
@@ -58,12 +63,7 @@ def x_ext_from_full(x: torch.Tensor, row0: int, Hb: int, R: int) -> torch.Tensor
     return x.index_select(2, idx).contiguous()
 
 
-def band_compute_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
-    """(U, Z, top, bot) of one band on its GPU via the C ABI.
-
-    x_ext: (B, C, Hb + 2R, W); w_band: (S*B, Cw, Hb, W).  U, Z: (B, C, Hb,
-    W) without the cross-band mirror terms; top / bot: (2, B, C, R, W)
-    mirror strips for the rows above / below the band."""
+def _band_args(x_ext, w_band, shifts):
     _require_cuda("accumulate_uz_band", x_ext, w_band)
     hs = _lib.host_shifts(shifts)
     R = int(hs.t[:, :2].abs().max())
@@ -73,20 +73,45 @@ def band_compute_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
     x_k = x_ext.to(xd).contiguous()
     w_k = w_band.to(wd).contiguous()
     acc = torch.float64 if xd == torch.float64 else torch.float32
+    return hs, R, B, C, Hb, W, xd, wd, x_k, w_k, acc
+
+
+def band_forward_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
+    """(U, Z) of one band without the cross-band mirror terms.
+    x_ext: (B, C, Hb + 2R, W) band rows with R halo rows above and below;
+    w_band: (S*B, Cw, Hb, W)."""
+    hs, R, B, C, Hb, W, xd, wd, x_k, w_k, acc = _band_args(x_ext, w_band, shifts)
     U = torch.empty((B, C, Hb, W), dtype=acc, device=x_ext.device)
     Z = torch.empty_like(U)
+    with torch.cuda.device(x_ext.device):
+        _lib.call("nsc_accumulate_uz_band_fwd", _lib.ptr(x_k), _lib.dtype_code(xd),
+                  _lib.ptr(w_k), _lib.dtype_code(wd), w_k.size(1), B, C, Hb, W,
+                  row0, Hg, hs.ptr, hs.S, _lib.ptr(U), _lib.ptr(Z),
+                  _lib.stream_of(x_ext))
+    return U, Z
+
+
+def band_edges_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
+    """(top, bot): the (2, B, C, R, W) mirror strips this band's weights
+    contribute to the R rows above / below it.  Reads only the band rows of
+    x_ext, so the halo rows may still be unset."""
+    hs, R, B, C, Hb, W, xd, wd, x_k, w_k, acc = _band_args(x_ext, w_band, shifts)
     top = torch.empty((2, B, C, R, W), dtype=acc, device=x_ext.device)
     bot = torch.empty_like(top)
-    with torch.cuda.device(x_ext.device):
-        st = _lib.stream_of(x_ext)
-        args = (_lib.ptr(x_k), _lib.dtype_code(xd), _lib.ptr(w_k),
-                _lib.dtype_code(wd), w_k.size(1), B, C, Hb, W, row0, Hg,
-                hs.ptr, hs.S)
-        _lib.call("nsc_accumulate_uz_band_fwd", *args, _lib.ptr(U),
-                  _lib.ptr(Z), st)
-        if R > 0:
-            _lib.call("nsc_accumulate_uz_band_edges", *args, _lib.ptr(top),
-                      _lib.ptr(bot), st)
+    if R > 0:
+        with torch.cuda.device(x_ext.device):
+            _lib.call("nsc_accumulate_uz_band_edges", _lib.ptr(x_k),
+                      _lib.dtype_code(xd), _lib.ptr(w_k), _lib.dtype_code(wd),
+                      w_k.size(1), B, C, Hb, W, row0, Hg, hs.ptr, hs.S,
+                      _lib.ptr(top), _lib.ptr(bot), _lib.stream_of(x_ext))
+    return top, bot
+
+
+def band_compute_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
+    """(U, Z, top, bot) of one band on its GPU via the C ABI (forward and
+    edge strips; see band_forward_cuda / band_edges_cuda)."""
+    top, bot = band_edges_cuda(x_ext, w_band, shifts, row0, Hg)
+    U, Z = band_forward_cuda(x_ext, w_band, shifts, row0, Hg)
     return U, Z, top, bot
 
 
@@ -94,7 +119,20 @@ def _add_strips(U, Z, from_below: Optional[torch.Tensor],
                 from_above: Optional[torch.Tensor]):
     """Add a neighbour's mirror strips: `from_below` (the lower band's top
     strip) lands on this band's last R rows, `from_above` (the upper band's
-    bottom strip) on its first R rows."""
+    bottom strip) on its first R rows.  CUDA tensors: one launch of
+    nsc_accumulate_uz_band_add_strips."""
+    strips = [t for t in (from_below, from_above) if t is not None]
+    if (U.is_cuda and strips and U.is_contiguous() and Z.is_contiguous()
+            and all(t.is_contiguous() and t.dtype == U.dtype for t in strips)):
+        B, C, Hb, W = U.shape
+        R = strips[0].shape[3]
+        with torch.cuda.device(U.device):
+            _lib.call("nsc_accumulate_uz_band_add_strips", _lib.ptr(U), _lib.ptr(Z),
+                      _lib.dtype_code(U.dtype), B, C, Hb, W, R,
+                      _lib.ptr(from_above) if from_above is not None else None,
+                      _lib.ptr(from_below) if from_below is not None else None,
+                      _lib.stream_of(U))
+        return U, Z
     if from_below is not None:
         R = from_below.shape[3]
         U[:, :, -R:] += from_below[0]
@@ -127,82 +165,91 @@ def accumulate_uz_banded_local(x, w, shifts, nbands: int,
     return (torch.cat([u for u, _ in res], 2), torch.cat([z for _, z in res], 2))
 
 
-def exchange_x_halo(x_band: torch.Tensor, R: int, group=None) -> torch.Tensor:
-    """Build this rank's (B, C, Hb + 2R, W) halo-extended band from its own
-    rows and its ring neighbours' edge rows (one grouped send/recv)."""
-    import torch.distributed as dist
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    if R == 0:
-        return x_band.contiguous()
-    if world == 1:
-        Hb = x_band.shape[2]
-        idx = torch.arange(-R, Hb + R, device=x_band.device) % Hb
-        return x_band.index_select(2, idx).contiguous()
-    up, down = (rank - 1) % world, (rank + 1) % world
-    first = x_band[:, :, :R].contiguous()
-    last = x_band[:, :, -R:].contiguous()
-    from_up = torch.empty_like(last)     # the upper band's last R rows
-    from_down = torch.empty_like(first)  # the lower band's first R rows
-    # With two ranks `up` and `down` are the same peer and messages between
-    # a pair match in issue order, so every rank sends its last rows before
-    # its first rows and receives from_up before from_down.
-    ops = [dist.P2POp(dist.isend, last, _g(down, group), group),
-           dist.P2POp(dist.isend, first, _g(up, group), group),
-           dist.P2POp(dist.irecv, from_up, _g(up, group), group),
-           dist.P2POp(dist.irecv, from_down, _g(down, group), group)]
-    for req in dist.batch_isend_irecv(ops):
-        req.wait()
-    return torch.cat([from_up, x_band, from_down], 2).contiguous()
-
-
 def _g(r, group):
     import torch.distributed as dist
     return r if group is None else dist.get_global_rank(group, r)
 
 
-def exchange_strips(top: torch.Tensor, bot: torch.Tensor, group=None):
-    """Send this band's mirror strips to the bands that own those rows and
-    receive theirs: returns (from_below, from_above), None at the image
-    edges (the mirror term is not periodic)."""
+def exchange_halo_and_strips(x_pad: torch.Tensor, R: int, top, bot, group=None):
+    """One grouped send/recv: fills the R halo rows of x_pad (rows [0, R)
+    and [R + Hb, Hb + 2R), band rows in between) from the ring neighbours,
+    sends this band's mirror strips and returns the neighbours' strips
+    (from_below, from_above), None at the image edges."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    ops: List = []
-    from_below = from_above = None
+    Hb = x_pad.shape[2] - 2 * R
+    if world == 1:
+        if R:
+            x_pad[:, :, :R] = x_pad[:, :, Hb:Hb + R]
+            x_pad[:, :, R + Hb:] = x_pad[:, :, R:2 * R]
+        return None, None
+    up, down = (rank - 1) % world, (rank + 1) % world
+    first = x_pad[:, :, R:2 * R].contiguous()      # this band's first R rows
+    last = x_pad[:, :, Hb:Hb + R].contiguous()     # this band's last R rows
+    from_up = torch.empty_like(last)
+    from_down = torch.empty_like(first)
+    from_above = torch.empty_like(bot) if rank > 0 else None
+    from_below = torch.empty_like(top) if rank + 1 < world else None
+    # Messages between a pair match in issue order (with two ranks `up` and
+    # `down` are the same peer): every rank sends last rows, first rows, top
+    # strip, bottom strip, and receives in the matching order.
+    ops = [dist.P2POp(dist.isend, last, _g(down, group), group),
+           dist.P2POp(dist.isend, first, _g(up, group), group)]
     if rank > 0:
-        ops.append(dist.P2POp(dist.isend, top.contiguous(), _g(rank - 1, group), group))
-        from_above = torch.empty_like(bot)
-        ops.append(dist.P2POp(dist.irecv, from_above, _g(rank - 1, group), group))
+        ops.append(dist.P2POp(dist.isend, top.contiguous(), _g(up, group), group))
     if rank + 1 < world:
-        ops.append(dist.P2POp(dist.isend, bot.contiguous(), _g(rank + 1, group), group))
-        from_below = torch.empty_like(top)
-        ops.append(dist.P2POp(dist.irecv, from_below, _g(rank + 1, group), group))
-    if ops:
-        for req in dist.batch_isend_irecv(ops):
-            req.wait()
+        ops.append(dist.P2POp(dist.isend, bot.contiguous(), _g(down, group), group))
+    ops += [dist.P2POp(dist.irecv, from_up, _g(up, group), group),
+            dist.P2POp(dist.irecv, from_down, _g(down, group), group)]
+    if from_above is not None:
+        ops.append(dist.P2POp(dist.irecv, from_above, _g(up, group), group))
+    if from_below is not None:
+        ops.append(dist.P2POp(dist.irecv, from_below, _g(down, group), group))
+    for req in dist.batch_isend_irecv(ops):
+        req.wait()
+    x_pad[:, :, :R] = from_up
+    x_pad[:, :, R + Hb:] = from_down
     return from_below, from_above
 
 
 def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
-                         compute: Callable = band_compute_cuda):
+                         compute: Optional[Callable] = None, *, padded: bool = False,
+                         forward: Callable = band_forward_cuda,
+                         edges: Callable = band_edges_cuda):
     """accumulate_uz of this rank's band of a row-split image.
 
-    x_band: (B, C, Hb, W) this rank's rows of x; w_band: (S*B, Cw, Hb, W)
-    this rank's rows of every weight plane; Hg: rows of the whole image.
-    Bands follow `band_rows(Hg, world, rank)` and must be at least R rows
-    tall.  Returns this band's (U, Z) rows."""
+    x_band: (B, C, Hb, W) this rank's rows of x -- or, with padded=True,
+    (B, C, Hb + 2R, W) with the band in rows [R, R + Hb) and R spare rows on
+    each side that this call overwrites with the halo; w_band: (S*B, Cw,
+    Hb, W) this rank's rows of every weight plane; Hg: rows of the whole
+    image.  Bands follow `band_rows(Hg, world, rank)` and must be at least R
+    rows tall.  Returns this band's (U, Z) rows.  `compute`, when given,
+    replaces both `forward` and `edges` with one call returning
+    (U, Z, top, bot) (run after the halo arrives)."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     row0, Hb = band_rows(Hg, world, rank)
-    if x_band.shape[2] != Hb:
-        raise RuntimeError(f"rank {rank}: band has {x_band.shape[2]} rows, "
-                           f"expected {Hb}")
     R = radius_of(shifts)
-    x_ext = exchange_x_halo(x_band, R, group)
-    U, Z, top, bot = compute(x_ext, w_band, shifts, row0, Hg)
+    if x_band.shape[2] != Hb + (2 * R if padded else 0):
+        raise RuntimeError(f"rank {rank}: band has {x_band.shape[2]} rows, "
+                           f"expected {Hb + (2 * R if padded else 0)}")
+    if padded:
+        x_pad = x_band
+    else:
+        x_pad = torch.empty((x_band.shape[0], x_band.shape[1], Hb + 2 * R,
+                             x_band.shape[3]), dtype=x_band.dtype,
+                            device=x_band.device)
+        x_pad[:, :, R:R + Hb] = x_band
+    if compute is not None:
+        def edges(xe, wb, sh, r0, hg):          # noqa: F811 (injected form)
+            return compute(xe, wb, sh, r0, hg)[2:]
+        def forward(xe, wb, sh, r0, hg):        # noqa: F811
+            return compute(xe, wb, sh, r0, hg)[:2]
+    top, bot = edges(x_pad, w_band, shifts, row0, Hg)
+    from_below, from_above = exchange_halo_and_strips(x_pad, R, top, bot, group)
+    U, Z = forward(x_pad, w_band, shifts, row0, Hg)
     if R == 0 or world == 1:
         return U, Z
-    from_below, from_above = exchange_strips(top, bot, group)
     return _add_strips(U, Z, from_below, from_above)

@@ -97,24 +97,43 @@ acc_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
 }
 
 // Mirror contributions of the band's own weights to the R rows outside it.
-// edge: (2, B, C, R, W); part 0 = U, part 1 = Z.  `top` selects the rows
-// above the band (targets row0-R .. row0-1) or below it.
+// Each strip is (2, B, C, R, W); part 0 = U, part 1 = Z; the top strip
+// targets rows row0-R .. row0-1, the bottom strip the R rows below the band.
+// Both strips in one launch, the shift loop split over kKS thread groups:
+// threadIdx.y takes every kKS-th shift and the partial sums meet in shared
+// memory.  blockIdx.y enumerates the 2R strip rows (top strip first).
+// The shifts that can reach each strip row (has_inv and a mirror source
+// row inside the band) are listed on the host, so a thread visits only
+// those: for row t above the band, rows with dx <= t; below, dx > t - Hb.
+constexpr int kKS = 8;
+constexpr int kEdgeRows = 64;        // 2R strip rows, R <= 32
+constexpr int kEdgeList = 4096;
+struct EdgeLists {
+    int32_t off[kEdgeRows + 1];      // row rr lists s[off[rr] .. off[rr+1])
+    int16_t s[kEdgeList];
+};
+
 template <typename TX, typename TW, int NC>
-__global__ void __launch_bounds__(kBX * kBY)
-acc_edge_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
-                typename Acc<TX>::type* __restrict__ edge, const ShiftTable st,
-                int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t Cw,
-                int64_t R, int64_t row0, int64_t Hg, int top, int64_t groups) {
+__global__ void __launch_bounds__(kBX * kKS)
+acc_edges2_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                  typename Acc<TX>::type* __restrict__ top_out,
+                  typename Acc<TX>::type* __restrict__ bot_out, const ShiftTable st,
+                  const EdgeLists lists,
+                  int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t Cw,
+                  int64_t R, int64_t row0, int64_t Hg, int64_t groups) {
     using A = typename Acc<TX>::type;
+    __shared__ A part[kKS][NC + 1][kBX];
     const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
-    const int64_t e = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
-    if (wcol >= W || e >= R) return;
-    const int64_t t = top ? (e - R) : (Hb + e);  // target row, band-local
+    const int k = threadIdx.y;
+    const bool top = blockIdx.y < R;
+    const int64_t e = top ? blockIdx.y : blockIdx.y - R;
+    const int64_t t = top ? (e - R) : (Hb + e);   // target row, band-local
     const int64_t plane_x = (Hb + 2 * R) * W;
     const int64_t plane_o = Hb * W;
     const int64_t plane_e = R * W;
     const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
-    const bool in_image = inb(row0 + t, Hg);
+    const bool active = wcol < W && inb(row0 + t, Hg);
+    A* out = top ? top_out : bot_out;
     for (int64_t g = blockIdx.z; g < groups; g += gridDim.z) {
         const int64_t b = g / cgroups;
         const int64_t cg = g % cgroups;
@@ -125,11 +144,13 @@ acc_edge_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
         A u[NC], z = A(0);
 #pragma unroll
         for (int i = 0; i < NC; ++i) u[i] = A(0);
-        if (in_image) {
-            for (int s = 0; s < st.S; ++s) {
-                if (!st.has_inv(s)) continue;
+        if (active) {
+            const int j1 = lists.off[blockIdx.y + 1];
+#pragma unroll 4
+            for (int j = lists.off[blockIdx.y] + k; j < j1; j += kKS) {
+                const int s = lists.s[j];
                 const int64_t hm = t - st.dx[s], wm = wcol - st.dy[s];
-                if (!inb(hm, Hb) || !inb(wm, W)) continue;
+                if (!inb(wm, W)) continue;
                 const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane_o;
                 const A mv = ldg_acc<TW, A>(ws + hm * W + wm);
                 const int64_t mo = (hm + R) * W + wm;
@@ -139,15 +160,46 @@ acc_edge_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                 z += mv;
             }
         }
-        const int64_t ob = (b * C + c0) * plane_e + e * W + wcol;
-        const int64_t zoff = B * C * plane_e;
+        __syncthreads();
 #pragma unroll
-        for (int i = 0; i < NC; ++i)
-            if (i < nc) {
-                edge[ob + i * plane_e] = u[i];
-                edge[zoff + ob + i * plane_e] = z;
+        for (int i = 0; i < NC; ++i) part[k][i][threadIdx.x] = u[i];
+        part[k][NC][threadIdx.x] = z;
+        __syncthreads();
+        if (k == 0 && wcol < W) {
+            A su[NC + 1];
+#pragma unroll
+            for (int i = 0; i <= NC; ++i) {
+                su[i] = A(0);
+                for (int j = 0; j < kKS; ++j) su[i] += part[j][i][threadIdx.x];
             }
+            const int64_t ob = (b * C + c0) * plane_e + e * W + wcol;
+            const int64_t zoff = B * C * plane_e;
+#pragma unroll
+            for (int i = 0; i < NC; ++i)
+                if (i < nc) {
+                    out[ob + i * plane_e] = su[i];
+                    out[zoff + ob + i * plane_e] = su[NC];
+                }
+        }
     }
+}
+
+// U/Z += neighbour strips; one thread per strip element and strip.
+template <typename A>
+__global__ void __launch_bounds__(256)
+band_add_strips_kernel(A* __restrict__ U, A* __restrict__ Z,
+                       const A* __restrict__ above, const A* __restrict__ below,
+                       int64_t planes, int64_t Hb, int64_t W, int64_t R) {
+    const int64_t n = planes * R * W;                 // elements per part
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= n) return;
+    const int64_t p = i / (R * W);
+    const int64_t rw = i - p * R * W;                  // r * W + w
+    const A* src = blockIdx.y == 0 ? above : below;
+    if (!src) return;
+    const int64_t dst = p * Hb * W + (blockIdx.y == 0 ? 0 : (Hb - R) * W) + rw;
+    U[dst] += src[i];
+    Z[dst] += src[n + i];
 }
 
 // Fused backward: thread owns pixel q and NC channels.
@@ -308,6 +360,27 @@ nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
                      int64_t Hg, const ShiftTable& st, void* top, void* bot,
                      cudaStream_t stream) {
     const int64_t R = st.R;
+    if (2 * R > kEdgeRows)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "accumulate_uz_band_edges: table radius %lld > %d", (long long)R,
+                    kEdgeRows / 2);
+    EdgeLists lists;
+    int n = 0;
+    for (int64_t rr = 0; rr < 2 * R; ++rr) {
+        lists.off[rr] = n;
+        const int64_t t = rr < R ? rr - R : Hb + (rr - R);   // band-local target row
+        for (int s = 0; s < st.S; ++s) {
+            if (!st.has_inv(s)) continue;
+            const int64_t hm = t - st.dx[s];
+            if (hm < 0 || hm >= Hb) continue;
+            if (n >= kEdgeList)
+                return fail(NSC_ERR_INVALID_ARG,
+                            "accumulate_uz_band_edges: more than %d (row, shift) "
+                            "pairs reach the strips", kEdgeList);
+            lists.s[n++] = static_cast<int16_t>(s);
+        }
+    }
+    lists.off[2 * R] = n;
     return with_types("accumulate_uz_band_edges", xd, wd, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
@@ -316,12 +389,12 @@ nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
         with_nc(C, Cw, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             const int64_t groups = n_groups(B, C, Cw, NC);
-            for (int t = 0; t < 2; ++t)
-                acc_edge_kernel<TX, TW, NC><<<grid_for(W, R, groups),
-                                               dim3(kBX, kBY), 0, stream>>>(
-                    static_cast<const TX*>(x), static_cast<const TW*>(w),
-                    static_cast<A*>(t ? top : bot), st, B, C, Hb, W, Cw, R, row0,
-                    Hg, t, groups);
+            const dim3 grid(grid_1d(W, kBX), static_cast<unsigned>(2 * R),
+                            static_cast<unsigned>(groups < 65535 ? groups : 65535));
+            acc_edges2_kernel<TX, TW, NC><<<grid, dim3(kBX, kKS), 0, stream>>>(
+                static_cast<const TX*>(x), static_cast<const TW*>(w),
+                static_cast<A*>(top), static_cast<A*>(bot), st, lists, B, C, Hb, W,
+                Cw, R, row0, Hg, groups);
         });
         return check_launch("accumulate_uz_band_edges");
     });
@@ -466,3 +539,29 @@ nsc_status nsc_accumulate_uz_band_edges(const void* x_ext, int x_dtype,
 }
 
 }  // extern "C"
+
+extern "C" nsc_status nsc_accumulate_uz_band_add_strips(
+    void* U, void* Z, int acc_dtype, int64_t B, int64_t C, int64_t Hb, int64_t W,
+    int64_t R, const void* strip_above, const void* strip_below, void* stream) {
+    using namespace nsc;
+    const char* op = "accumulate_uz_band_add_strips";
+    if (acc_dtype != NSC_F32 && acc_dtype != NSC_F64)
+        return fail(NSC_ERR_UNSUPPORTED_DTYPE, "%s: acc_dtype must be fp32 or fp64", op);
+    if (B < 0 || C < 0 || Hb < 0 || W < 0 || R < 0 || R > Hb)
+        return fail(NSC_ERR_INVALID_ARG, "%s: bad extents (R must be <= Hb)", op);
+    if (B == 0 || C == 0 || W == 0 || R == 0 || (!strip_above && !strip_below)) return ok();
+    if (!U || !Z) return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
+    const int64_t n = B * C * R * W;
+    const dim3 grid(grid_1d(n, 256), 2);
+    if (acc_dtype == NSC_F32)
+        band_add_strips_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(
+            static_cast<float*>(U), static_cast<float*>(Z),
+            static_cast<const float*>(strip_above), static_cast<const float*>(strip_below),
+            B * C, Hb, W, R);
+    else
+        band_add_strips_kernel<double><<<grid, 256, 0, as_stream(stream)>>>(
+            static_cast<double*>(U), static_cast<double*>(Z),
+            static_cast<const double*>(strip_above), static_cast<const double*>(strip_below),
+            B * C, Hb, W, R);
+    return check_launch(op);
+}

@@ -1,7 +1,8 @@
 """Row-band split of accumulate_uz across ranks, on CPU `gloo` ranks.
 
 The exchange logic of neural_shift_cuda_b200.bands (x-halo ring and
-mirror-strip exchange) runs unchanged; only the per-band compute is a CPU
+mirror-strip exchange in one grouped send/recv, plain and padded x bands)
+runs unchanged; only the per-band compute is a CPU
 restatement injected here, so no GPU is needed.  Every rank checks its
 band against the oracle's full-image result.
 """
@@ -59,7 +60,7 @@ def _band_compute_cpu(x_ext, w_band, shifts, row0, Hg):
     return U, Z, top, bot
 
 
-def _worker(rank, world, port, Hg, W, R, out):
+def _worker(rank, world, port, Hg, W, R, padded, out):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -73,10 +74,14 @@ def _worker(rank, world, port, Hg, W, R, out):
                                            dtype=torch.float64), sh, B)
         U_ref, Z_ref = O.accumulate_uz(x, w.expand(-1, C, -1, -1), sh)
         row0, Hb = bands.band_rows(Hg, world, rank)
+        xb = x[:, :, row0:row0 + Hb].contiguous()
+        if padded:   # spare halo rows hold NaN: the exchange must overwrite them
+            xp = torch.full((B, C, Hb + 2 * R, W), float("nan"), dtype=x.dtype)
+            xp[:, :, R:R + Hb] = xb
+            xb = xp
         U, Z = bands.accumulate_uz_banded(
-            x[:, :, row0:row0 + Hb].contiguous(),
-            w[:, :, row0:row0 + Hb].contiguous(), sh, Hg,
-            compute=_band_compute_cpu)
+            xb, w[:, :, row0:row0 + Hb].contiguous(), sh, Hg,
+            compute=_band_compute_cpu, padded=padded)
         ok = (torch.allclose(U, U_ref[:, :, row0:row0 + Hb], rtol=1e-10, atol=1e-10)
               and torch.allclose(Z, Z_ref[:, :, row0:row0 + Hb], rtol=1e-10, atol=1e-10))
         out[rank] = 1 if ok else 0
@@ -92,11 +97,13 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("world,Hg,W,R", [(2, 12, 9, 2), (3, 17, 7, 3), (2, 8, 6, 1)])
-def test_banded_accumulate_gloo(world, Hg, W, R):
+@pytest.mark.parametrize("world,Hg,W,R,padded", [(2, 12, 9, 2, False), (3, 17, 7, 3, False),
+                                                 (2, 8, 6, 1, False), (3, 17, 7, 3, True),
+                                                 (2, 12, 9, 2, True)])
+def test_banded_accumulate_gloo(world, Hg, W, R, padded):
     ctx = mp.get_context("spawn")
     out = ctx.Array("i", [0] * world)
-    mp.start_processes(_worker, args=(world, _free_port(), Hg, W, R, out),
+    mp.start_processes(_worker, args=(world, _free_port(), Hg, W, R, padded, out),
                        nprocs=world, join=True, start_method="spawn")
     assert list(out) == [1] * world
 

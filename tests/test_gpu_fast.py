@@ -147,3 +147,34 @@ def test_fullsize_config5_properties(cuda):
                                rtol=1e-5, atol=1e-4)
     del xc, wc
     assert _lib.wait_timeouts() == 0
+
+
+@pytest.mark.parametrize("padded", [False, True])
+def test_banded_single_rank_process_group(cuda, padded):
+    """accumulate_uz_banded through a one-rank process group: the halo is
+    the band's own circular wrap and no strips travel; the result equals
+    the unsplit op (plain and padded x buffers)."""
+    import os
+    import torch.distributed as dist
+    from neural_shift_cuda_b200 import bands
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29561")
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        torch.manual_seed(4)
+        R = 3
+        sh = T(O.halfplane_shifts(R))
+        S = len(sh)
+        x = torch.rand(1, 3, 40, 64, dtype=torch.float16)
+        w = torch.rand(S, 1, 40, 64, dtype=torch.float16)
+        U0, Z0 = nsc.accumulate_uz(x.to(cuda), w.to(cuda), sh)
+        xb = x.to(cuda)
+        if padded:
+            xp = torch.full((1, 3, 40 + 2 * R, 64), float("nan"), dtype=x.dtype, device=cuda)
+            xp[:, :, R:R + 40] = xb
+            xb = xp
+        U, Z = bands.accumulate_uz_banded(xb, w.to(cuda), sh, 40, padded=padded)
+        torch.testing.assert_close(U, U0, rtol=1e-6, atol=1e-5)
+        torch.testing.assert_close(Z, Z0, rtol=1e-6, atol=1e-5)
+    finally:
+        dist.destroy_process_group()
