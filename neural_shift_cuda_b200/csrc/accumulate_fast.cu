@@ -20,8 +20,7 @@ namespace nsc {
 namespace fast {
 
 template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
-bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x,
-            void* U, void* Z,
+bool launch(const WMaps& maps, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
             cudaStream_t stream);
 
@@ -47,10 +46,10 @@ int sm_count() {
 }
 
 template <typename T, int NC>
-bool by_bucket(bool exact, int K, const CUtensorMap& map, const CUtensorMap& map2,
+bool by_bucket(bool exact, int K, const fast::WMaps& maps,
                const void* x, void* U, void* Z, const fast::FastTable& tab,
                const fast::Geo& g, unsigned int* to, cudaStream_t st) {
-#define NSC_B(A, B, E) return fast::launch<T, NC, A, B, E>(map, map2, x, U, Z, tab, g, to, st)
+#define NSC_B(A, B, E) return fast::launch<T, NC, A, B, E>(maps, x, U, Z, tab, g, to, st)
     if (exact) {
         switch (K) {
             case 2: NSC_B(0, 2, true);
@@ -108,27 +107,57 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
         rx = (dx < 0 ? -dx : dx) > rx ? (dx < 0 ? -dx : dx) : rx;
     }
     tab.Rx = rx;
-    // Pair consecutive entries of the visiting order ((dx, dy) ascending)
-    // that are consecutive weight planes (s, s+1) with the same box origin:
-    // one TMA copy then carries both planes.
+    // Copy size: up to kGroup planes, fewer when three such stages would not
+    // fit next to the x tiles (the launcher needs at least three stages);
+    // tables grouped below kGroup take the mask-driven (non-EXACT) kernel.
+    int group_cap = kGroup;
+    {
+        const int span = dymax > -dymin ? dymax : -dymin;
+        const int Kmax = span <= 4 ? 4 : span <= 8 ? 8 : span <= 12 ? 12 : 16;
+        const int XCg = align_up(Kmax, V);
+        const size_t plane = static_cast<size_t>(TH + rx) * (TPR * V + XCg) * es;
+        const size_t xt = static_cast<size_t>(NSC_FAST_XBUF) * NC * (TH + 2 * rx) *
+                          (TPR * V + 2 * XCg) * es + 16 + 4 * 16 + 16 + 128;
+        while (group_cap > 1 &&
+               xt + 3 * (((group_cap * plane + 127) & ~size_t(127)) + 16) > 227u * 1024u)
+            --group_cap;
+    }
+    // Group consecutive entries of the visiting order ((dx, dy) ascending)
+    // that are consecutive weight planes (s, s+1, ...) with the same box
+    // origin, up to kGroup planes: one TMA copy then carries the group.
+    int gmax = 1;
+    int8_t pos[2 * MAXR + 1][2 * MAXR + 1];
+    bool lastp[2 * MAXR + 1][2 * MAXR + 1];
     for (int dx = -rx; dx <= rx; ++dx) {
-        int prev = -1, prev_dy = 0;
+        int start_dy = 0, len = 0, prev_s = -2, prev_mo = -1;
+        auto close = [&]() {
+            if (len == 0) return;
+            int16_t& e0 = tab.s[dx + MAXR][start_dy + MAXR];
+            e0 = static_cast<int16_t>(e0 | (len << kLenShift));
+            gmax = len > gmax ? len : gmax;
+        };
+        int prev_dy = 0;
         for (int dy = -MAXR; dy <= MAXR; ++dy) {
-            int16_t& e = tab.s[dx + MAXR][dy + MAXR];
+            const int16_t e = tab.s[dx + MAXR][dy + MAXR];
             if (e < 0) continue;
             const int mo = dy > 0 ? (dy + V - 1) / V * V : 0;
-            const int pmo = prev_dy > 0 ? (prev_dy + V - 1) / V * V : 0;
-            if (prev >= 0 && NSC_FAST_PAIRS) {
-                int16_t& pe = tab.s[dx + MAXR][prev_dy + MAXR];
-                if (!(pe & (kPairFirst | kPairSecond)) && (e & kSMask) == (pe & kSMask) + 1 &&
-                    mo == pmo) {
-                    pe = static_cast<int16_t>(pe | kPairFirst);
-                    e = static_cast<int16_t>(e | kPairSecond);
-                }
+            const int sv = e & kSMask;
+            if (len > 0 && len < group_cap && sv == prev_s + 1 && mo == prev_mo) {
+                pos[dx + MAXR][dy + MAXR] = static_cast<int8_t>(len);
+                lastp[dx + MAXR][prev_dy + MAXR] = false;
+                ++len;
+            } else {
+                close();
+                start_dy = dy;
+                len = 1;
+                pos[dx + MAXR][dy + MAXR] = 0;
             }
-            prev = e;
+            lastp[dx + MAXR][dy + MAXR] = true;
+            prev_s = sv;
+            prev_mo = mo;
             prev_dy = dy;
         }
+        close();
     }
     for (int dx = -MAXR; dx <= MAXR; ++dx)
         for (int dy = -MAXR; dy <= MAXR; ++dy) {
@@ -137,11 +166,12 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
             const uint64_t bit = 1ull << (dy + MAXR);
             tab.present[dx + MAXR] |= bit;
             if (e & kInvBit) tab.inv[dx + MAXR] |= bit;
-            if (e & kPairFirst) tab.first[dx + MAXR] |= bit;
-            if (e & kPairSecond) tab.second[dx + MAXR] |= bit;
+            if (pos[dx + MAXR][dy + MAXR] & 1) tab.pos0[dx + MAXR] |= bit;
+            if (pos[dx + MAXR][dy + MAXR] & 2) tab.pos1[dx + MAXR] |= bit;
+            if (lastp[dx + MAXR][dy + MAXR]) tab.last[dx + MAXR] |= bit;
         }
     // Canonical half-plane table of radius R: compile-time entry pattern.
-    bool exact = dymin >= 0 && dymax == rx && rx >= 1;
+    bool exact = dymin >= 0 && dymax == rx && rx >= 1 && group_cap == kGroup;
     for (int dx = -rx; exact && dx <= rx; ++dx)
         for (int dy = 0; dy <= rx; ++dy) {
             const int e = tab.s[dx + MAXR][dy + MAXR];
@@ -149,11 +179,12 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
             if ((e >= 0) != want) { exact = false; break; }
             if (e < 0) continue;
             const bool inv = e & kInvBit;
-            const bool first = e & kPairFirst, second = e & kPairSecond;
+            const int p = pos[dx + MAXR][dy + MAXR];
+            const bool l = lastp[dx + MAXR][dy + MAXR];
             const bool want_inv = dy > 0 || dx != 0;
-            const bool want_first = NSC_FAST_PAIRS && dy > 0 && (dy & 1) && dy < rx;
-            const bool want_second = NSC_FAST_PAIRS && dy > 0 && !(dy & 1);
-            if (inv != want_inv || first != want_first || second != want_second) {
+            const int want_p = dy > 0 ? (dy - 1) % kGroup : 0;
+            const bool want_l = dy == 0 || want_p == kGroup - 1 || dy == rx;
+            if (inv != want_inv || p != want_p || l != want_l) {
                 exact = false;
                 break;
             }
@@ -194,23 +225,24 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                                    : xd == NSC_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     g.plane_bytes = g.stage_tx;
-    g.stage_stride = (2 * g.stage_tx + 127u) & ~127u;   // room for a pair
-    CUtensorMap map, map2;
+    g.stage_stride = (static_cast<uint32_t>(gmax) * g.stage_tx + 127u) & ~127u;
+    WMaps maps;
     const char* err = nullptr;
-    if (!encode_map_4d(&map, w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH, 1, &err) ||
-        !encode_map_4d(&map2, w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH, 2, &err))
-        DECLINE("tensor map");
+    for (int d = 1; d <= 4; ++d)
+        if (!encode_map_4d(&maps.m[d - 1], w, es, dt, W, Hout, B * Cw, st.S, g.BW, g.BH,
+                           d <= st.S ? d : 1, &err))
+            DECLINE("tensor map");
     unsigned int* to = wait_timeout_counter();
     if (!to) DECLINE("timeout counter");
     (void)sm_count;
     if (xd == NSC_F16)
-        return NC == 1 ? by_bucket<__half, 1>(exact, K, map, map2, x, U, Z, tab, g, to, stream)
-                       : by_bucket<__half, 3>(exact, K, map, map2, x, U, Z, tab, g, to, stream);
+        return NC == 1 ? by_bucket<__half, 1>(exact, K, maps, x, U, Z, tab, g, to, stream)
+                       : by_bucket<__half, 3>(exact, K, maps, x, U, Z, tab, g, to, stream);
     if (xd == NSC_BF16)
-        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(exact, K, map, map2, x, U, Z, tab, g, to, stream)
-                       : by_bucket<__nv_bfloat16, 3>(exact, K, map, map2, x, U, Z, tab, g, to, stream);
-    return NC == 1 ? by_bucket<float, 1>(exact, K, map, map2, x, U, Z, tab, g, to, stream)
-                   : by_bucket<float, 3>(exact, K, map, map2, x, U, Z, tab, g, to, stream);
+        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(exact, K, maps, x, U, Z, tab, g, to, stream)
+                       : by_bucket<__nv_bfloat16, 3>(exact, K, maps, x, U, Z, tab, g, to, stream);
+    return NC == 1 ? by_bucket<float, 1>(exact, K, maps, x, U, Z, tab, g, to, stream)
+                   : by_bucket<float, 3>(exact, K, maps, x, U, Z, tab, g, to, stream);
 }
 
 int fast_sm_count() { return sm_count(); }

@@ -13,12 +13,15 @@
 // (h0 - max(dx, 0), w0 - align_up(max(dy, 0))), so both reads hit shared
 // memory and each weight byte leaves HBM once (the overlap with the
 // neighbouring tiles is served by L2).  Out-of-image box parts are filled
-// with zeros by TMA, which is exactly the mirror term's mask.  The boxes
-// stream through an NSTAGE-deep ring of full/empty mbarriers.
+// with zeros by TMA, which is exactly the mirror term's mask.  Up to four
+// consecutive planes with the same box origin (dy 1..4, 5..8, ... of a
+// canonical table) travel in one 4-D copy, so a full/empty mbarrier
+// handshake covers four shifts; the copies stream through an NSTAGE-deep
+// ring.
 //
 // Image.  Per tile the consumers stage a halo tile of x with circular
-// rows/columns in shared memory (double-buffered: the next tile's copy is
-// issued with cp.async while this one computes).  Shifts are visited grouped
+// rows/columns in shared memory (cp.async; one buffer, refilled at the tile
+// boundary, which leaves room for a deeper weight ring).  Shifts are visited grouped
 // by dx; for one dx every thread loads register windows of its forward row
 // (h + dx) and mirror row (h - dx) once and serves every dy of the group with
 // compile-time register indices (dy is a template-unrolled loop); on tiles
@@ -42,13 +45,15 @@
 #ifndef NSC_FAST_EXPERIMENT
 #define NSC_FAST_EXPERIMENT 0
 #endif
-// 1: two consecutive shifts share one weight copy (canonical tables)
-#ifndef NSC_FAST_PAIRS
-#define NSC_FAST_PAIRS 1
+// Up to this many consecutive weight planes (same dx, consecutive plane
+// index, same box origin) travel in one TMA copy.
+#ifndef NSC_FAST_GROUP
+#define NSC_FAST_GROUP 4
 #endif
-// x halo tile buffers: 2 = the next tile's x is prefetched during this one
+// x halo tile buffers: 2 = the next tile's x is prefetched during this one;
+// 1 = one buffer (refilled at the tile boundary), more room for weights
 #ifndef NSC_FAST_XBUF
-#define NSC_FAST_XBUF 2
+#define NSC_FAST_XBUF 1
 #endif
 
 #include "nsc_common.cuh"
@@ -70,16 +75,23 @@ constexpr int MAXSTAGE = 16;     // ring depth is chosen per launch (<= this)
 constexpr int STRIP = NSC_FAST_STRIP;   // tile columns per raster strip
 constexpr int MAXR = 16;        // |dx|, |dy| <= MAXR on this path
 constexpr int kInvBit = 0x800;       // row has a mirror term
-constexpr int kPairFirst = 0x1000;   // shares its weight copy with the next entry
-constexpr int kPairSecond = 0x2000;  // second plane of the previous entry's copy
+constexpr int kLenShift = 12;        // bits 12-14: planes in the copy this entry
+                                     // starts (1..4), 0 for a later member
 constexpr int kSMask = 0x7FF;
+constexpr int kGroup = NSC_FAST_GROUP;
+static_assert(kGroup >= 1 && kGroup <= 4, "copies carry 1 to 4 planes");
+
+// Box-depth 1..4 tensor maps of the weight stack.
+struct WMaps {
+    CUtensorMap m[4];
+};
 
 struct FastTable {
     int16_t s[2 * MAXR + 1][2 * MAXR + 1];  // [dx+MAXR][dy+MAXR] -> s | flags, or -1
     // per dx row, bit (dy + MAXR): entry present / has a mirror term /
-    // first of a paired copy / second of a paired copy
+    // position of its plane in its copy (two bits) / last plane of its copy
     uint64_t present[2 * MAXR + 1], inv[2 * MAXR + 1];
-    uint64_t first[2 * MAXR + 1], second[2 * MAXR + 1];
+    uint64_t pos0[2 * MAXR + 1], pos1[2 * MAXR + 1], last[2 * MAXR + 1];
     uint8_t row_any[2 * MAXR + 1];
     uint8_t row_inv[2 * MAXR + 1];
     int32_t Rx;                             // max |dx|
@@ -335,12 +347,11 @@ __device__ __forceinline__ void load_win(uint32_t (&d)[N], const uint32_t* p) {
 // EXACT: the table is the canonical half-plane table of radius Rdy <= DYMAX
 // (for every dx: dy = 1..Rdy with mirror terms, plus (dx, 0) for dx >= 0
 // with a mirror term for dx != 0; weight planes consecutive along dy), so
-// which entries exist, which have a mirror term and how they pair into
+// which entries exist, which have a mirror term and how they group into
 // copies are compile-time facts of dy and need no per-shift table tests.
 template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
 __global__ void __launch_bounds__(NTHREADS, 1)
-acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
-                const __grid_constant__ CUtensorMap wmap2, const T* __restrict__ x,
+acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 float* __restrict__ U, float* __restrict__ Zo, const FastTable tab,
                 const Geo g, unsigned int* timeouts,
                 unsigned long long* __restrict__ ticket) {
@@ -419,7 +430,8 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                 if (!tab.row_any[dx + MAXR]) continue;
                 for (int dy = DYMIN; dy <= DYMAX; ++dy) {
                     const int e = tab.s[dx + MAXR][dy + MAXR];
-                    if (e < 0 || (e & kPairSecond)) continue;
+                    const int len = (e >> kLenShift) & 7;
+                    if (e < 0 || len == 0) continue;
                     const int s = e & kSMask;
                     if (!mbar_wait(&empty[stage], phase ^ 1u, timeouts) ||
                         *(volatile int*)&abort_flag) {
@@ -427,19 +439,20 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         *(volatile int*)&abort_flag = 1;
                         break;
                     }
-                    const bool pair = e & kPairFirst;
                     if (NSC_FAST_EXPERIMENT == 4) {   // handshake without a copy
                         mbar_arrive(&full[stage]);
                         ++it;
                         if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
                         continue;
                     }
-                    mbar_arrive_expect_tx(&full[stage], pair ? 2 * g.plane_bytes
-                                                             : g.plane_bytes);
+                    mbar_arrive_expect_tx(&full[stage], len * g.plane_bytes);
                     const int mo = dy > 0 ? align_up(dy, V) : 0;
                     // weight plane (s, b, wc) is slice s of the (B*Cw) index
-                    // b * Cw + wc; a pair copies slices s and s + 1.
-                    tma_load_4d(stages + stage * g.stage_stride, pair ? &wmap2 : &wmap1,
+                    // b * Cw + wc; a copy of `len` planes takes s .. s+len-1.
+                    const CUtensorMap* map = len == 1 ? &wmaps.m[0]
+                                             : len == 2 ? &wmaps.m[1]
+                                             : len == 3 ? &wmaps.m[2] : &wmaps.m[3];
+                    tma_load_4d(stages + stage * g.stage_stride, map,
                                 &full[stage], w0 - mo, h0 - (dx > 0 ? dx : 0),
                                 static_cast<int32_t>(b * g.Cw + wc), s);
                     ++it;
@@ -604,14 +617,17 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             const uint32_t off_main = static_cast<uint32_t>((mrow0 * BW + tc * V) * sizeof(T));
             const uint32_t off_mir = static_cast<uint32_t>(((mrow0 - dx) * BW + tc * V) * sizeof(T));
             const uint64_t m_pres = tab.present[dx + MAXR], m_inv = tab.inv[dx + MAXR];
-            const uint64_t m_first = tab.first[dx + MAXR], m_second = tab.second[dx + MAXR];
+            const uint64_t m_pos0 = tab.pos0[dx + MAXR], m_pos1 = tab.pos1[dx + MAXR];
+            const uint64_t m_last = tab.last[dx + MAXR];
             uint32_t stp = stages32 + stage * g.stage_stride;
-            auto one = [&](auto dyc, const bool second, const bool first, const bool inv) {
+            // pos: plane of this entry inside its copy (the copy's first
+            // entry waits for it); last: the copy is released afterwards
+            auto one = [&](auto dyc, const int pos, const bool last, const bool inv) {
                 constexpr int dy = decltype(dyc)::value;
-                if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && !second)
+                if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && pos == 0)
                     mbar_wait32_ab(full32 + 8 * stage, phase, timeouts,
                                    (volatile int*)&abort_flag);
-                const uint32_t sp = after(second ? stp + g.plane_bytes : stp);
+                const uint32_t sp = after(stp) + pos * g.plane_bytes;
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
                 lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
@@ -642,7 +658,7 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
                         add_e<T, kk + i>(z[i], mw);
                     });
                 }
-                if (!first) {   // copy fully used: release it
+                if (last) {   // copy fully used: release it
                     __syncwarp();
                     if (lane == 0 && NSC_FAST_EXPERIMENT != 6) mbar_arrive32(empty32 + 8 * stage);
                     if (++stage == NSTAGE) {
@@ -656,27 +672,24 @@ acc_fast_kernel(const __grid_constant__ CUtensorMap wmap1,
             };
             if constexpr (EXACT) {
                 // (dx, 0): a single copy, mirror term unless dx == 0
-                if (dx >= 0) one(std::integral_constant<int, 0>{}, false, false, dx != 0);
+                if (dx >= 0) one(std::integral_constant<int, 0>{}, 0, true, dx != 0);
                 const int R = tab.Rdy;
-                // dy = 1..R: (odd, even) pairs share a copy; a trailing odd
-                // dy (R odd) is single.
+                // dy = 1..R: copies of kGroup planes, dy 1..kGroup,
+                // kGroup+1..2 kGroup, ...; the last copy ends at dy = R.
                 static_for<1, DYMAX + 1>([&](auto jc) {
                     constexpr int dy = decltype(jc)::value;
                     if (dy > R) return;
-                    if constexpr (!NSC_FAST_PAIRS)
-                        one(jc, false, false, true);
-                    else if constexpr (dy & 1)
-                        one(jc, false, dy < R, true);
-                    else
-                        one(jc, true, false, true);
+                    constexpr int p = (dy - 1) % kGroup;
+                    one(jc, p, p == kGroup - 1 || dy == R, true);
                 });
             } else {
                 static_for<0, NDY>([&](auto jc) {
                     constexpr int dy = DYMIN + decltype(jc)::value;
                     constexpr int bit = dy + MAXR;
                     if (!((m_pres >> bit) & 1u)) return;
-                    one(std::integral_constant<int, dy>{}, (m_second >> bit) & 1u,
-                        (m_first >> bit) & 1u, (m_inv >> bit) & 1u);
+                    one(std::integral_constant<int, dy>{},
+                        static_cast<int>(((m_pos0 >> bit) & 1u) | (((m_pos1 >> bit) & 1u) << 1)),
+                        (m_last >> bit) & 1u, (m_inv >> bit) & 1u);
                 });
             }
         }

@@ -2,4 +2,5 @@
 #include "accumulate_fast_launch.cuh"
 using nsc::fast::FastTable;
 using nsc::fast::Geo;
+using nsc::fast::WMaps;
 NSC_FAST_INSTANTIATE(__half, 1)

@@ -15,7 +15,7 @@ void fast_set_decline(const char* why);
 namespace fast {
 
 template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
-bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, void* U, void* Z,
+bool launch(const WMaps& maps, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
             cudaStream_t stream) {
     unsigned long long* ticket = tile_ticket(stream);
@@ -57,7 +57,7 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
     }
     const int64_t nsm = fast_sm_count();
     const unsigned grid = static_cast<unsigned>(g.ntiles < nsm ? g.ntiles : nsm);
-    k<<<grid, NTHREADS, smem, stream>>>(map1, map2, static_cast<const T*>(x),
+    k<<<grid, NTHREADS, smem, stream>>>(maps, static_cast<const T*>(x),
                                         static_cast<float*>(U),
                                         static_cast<float*>(Z), tab, g, timeouts, ticket);
     return true;
@@ -67,8 +67,8 @@ bool launch(const CUtensorMap& map1, const CUtensorMap& map2, const void* x, voi
 }  // namespace nsc
 
 #define NSC_FAST_ONE(T, NC, A, B, E)                                               \
-    template bool nsc::fast::launch<T, NC, A, B, E>(const CUtensorMap&,              \
-        const CUtensorMap&, const void*, void*, void*, const FastTable&, Geo,        \
+    template bool nsc::fast::launch<T, NC, A, B, E>(const WMaps&,                    \
+        const void*, void*, void*, const FastTable&, Geo,                            \
         unsigned int*, cudaStream_t);
 #define NSC_FAST_INSTANTIATE(T, NC)                                                  \
     NSC_FAST_ONE(T, NC, 0, 2, true) NSC_FAST_ONE(T, NC, 0, 4, true)                  \
