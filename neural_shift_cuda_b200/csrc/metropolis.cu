@@ -365,7 +365,8 @@ inline dim3 tile_grid(const mtile::Geo& g) {
                 static_cast<unsigned>(g.groups < 65535 ? g.groups : 65535));
 }
 
-// Dynamic shared memory of a tiled kernel with `planes` staged planes.
+// Dynamic shared memory of a tiled kernel staging `planes` values (one
+// record of that many) per halo pixel.
 template <typename K>
 bool tile_smem(K kern, const mtile::Geo& g, int planes, size_t elem, size_t* bytes) {
     *bytes = static_cast<size_t>(planes) * g.XR * g.XP * elem;
@@ -407,7 +408,7 @@ nsc_status nsc_metropolis_fwd(const void* w_half, int w_dtype, int64_t w_channel
                 constexpr int NC = decltype(tag)::value_nc;
                 auto agg = mtile::aggregate_tile<T, NC>;
                 size_t smem = 0;
-                if (!tile_smem(agg, tg, 1 + NC, sizeof(A), &smem)) return;
+                if (!tile_smem(agg, tg, mtile::kAggF<A, NC>, sizeof(A), &smem)) return;
                 mtile::degree_tile<T><<<tile_grid(tg), dim3(mtile::TX, mtile::TY), 0, sm>>>(
                     static_cast<const T*>(w_half), static_cast<A*>(degree), st, tg,
                     use_box ? 1 : 0);
@@ -466,8 +467,8 @@ nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype, int64_t w_channel
                 auto ka = mtile::bwd_a_tile<T, NC>;
                 auto kb = mtile::bwd_b_tile<T, NC>;
                 size_t sa = 0, sb = 0;
-                if (!tile_smem(ka, tg, 3 + 2 * NC, sizeof(A), &sa) ||
-                    !tile_smem(kb, tg, 4 + 2 * NC, sizeof(A), &sb))
+                if (!tile_smem(ka, tg, mtile::kBwdAF<A, NC>, sizeof(A), &sa) ||
+                    !tile_smem(kb, tg, mtile::kBwdBF<A, NC>, sizeof(A), &sb))
                     return;
                 ka<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sa, sm>>>(
                     static_cast<const T*>(w_half), static_cast<const T*>(img),

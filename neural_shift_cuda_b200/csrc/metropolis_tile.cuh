@@ -112,6 +112,24 @@ __device__ __forceinline__ EdgeGeom edge_geom(const Geo& g, int h, int w, int dx
     return e;
 }
 
+// Per-pixel records of the staged halo: the quantities one edge reads at a
+// neighbour sit together, so a neighbour costs one address and a few
+// 16-byte loads.  Records are padded to 16 bytes.
+template <typename A>
+__host__ __device__ constexpr int rec_len(int n) {
+    return sizeof(A) == 4 ? (n + 3) / 4 * 4 : (n + 1) / 2 * 2;
+}
+template <typename A, int F>
+struct alignas(16) Rec {
+    A f[F];
+};
+// aggregation: r, x[NC]
+template <typename A, int NC> constexpr int kAggF = rec_len<A>(1 + NC);
+// backward A: d, r, a, x[NC], gWx[NC]
+template <typename A, int NC> constexpr int kBwdAF = rec_len<A>(3 + 2 * NC);
+// backward B: d, r, a, g_d, x[NC], gWx[NC]
+template <typename A, int NC> constexpr int kBwdBF = rec_len<A>(4 + 2 * NC);
+
 // ---------------------------------------------------------------- degree
 template <typename T>
 __global__ void __launch_bounds__(NT)
@@ -170,10 +188,9 @@ aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
                T* __restrict__ dhat, const ShiftTable st, const Geo g, int use_box,
                typename Acc<T>::type eps) {
     using A = typename Acc<T>::type;
+    constexpr int F = kAggF<A, NC>;
     extern __shared__ __align__(16) unsigned char smem_m[];
-    const int PL = g.XR * g.XP;
-    A* sr = reinterpret_cast<A*>(smem_m);     // 1 / max(d, eps)
-    A* sx = sr + PL;                          // [NC]
+    Rec<A, F>* rec = reinterpret_cast<Rec<A, F>*>(smem_m);   // r, x[NC]
     const int64_t HW = static_cast<int64_t>(g.H) * g.W;
     const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
     for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
@@ -184,10 +201,14 @@ aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
             const A* dg = d + grp * HW;
             for_halo(g, o.h0, o.w0, [&](int idx, int64_t off) {
                 const A dv = dg[off];
-                sr[idx] = A(1) / (dv > eps ? dv : eps);
+                Rec<A, F> r;
+#pragma unroll
+                for (int k = 0; k < F; ++k) r.f[k] = A(0);
+                r.f[0] = A(1) / (dv > eps ? dv : eps);
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
-                    sx[c * PL + idx] = static_cast<A>(to_acc(x[cb + c * HW + off]));
+                    r.f[1 + c] = static_cast<A>(to_acc(x[cb + c * HW + off]));
+                rec[idx] = r;
             });
             __syncthreads();
             const int wcol = o.w0 + threadIdx.x;
@@ -200,7 +221,7 @@ aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
                 const int h = o.h0 + threadIdx.y + TY * p;
                 hh[p] = h < g.H ? h : g.H - 1;
                 ci[p] = (threadIdx.y + TY * p + g.R) * g.XP + threadIdx.x + g.R;
-                ri[p] = sr[ci[p]];
+                ri[p] = rec[ci[p]].f[0];
                 dh[p] = A(0);
 #pragma unroll
                 for (int c = 0; c < NC; ++c) kx[p][c] = A(0);
@@ -219,17 +240,17 @@ aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
                         const A wq = ldg_acc<T, A>(ws + e.q);
                         const A wm = ldg_acc<T, A>(ws + e.m);
                         if (!use_box || e.in_p) {
-                            const int n = ci[p] + off;
-                            const A wk = wq * amin(ri[p], sr[n]);
+                            const Rec<A, F> nb = rec[ci[p] + off];
+                            const A wk = wq * amin(ri[p], nb.f[0]);
 #pragma unroll
-                            for (int c = 0; c < NC; ++c) kx[p][c] += wk * sx[c * PL + n];
+                            for (int c = 0; c < NC; ++c) kx[p][c] += wk * nb.f[1 + c];
                             dh[p] += wk;
                         }
                         if (inv && (!use_box || e.in_m)) {
-                            const int n = ci[p] - off;
-                            const A wk = wm * amin(ri[p], sr[n]);
+                            const Rec<A, F> nb = rec[ci[p] - off];
+                            const A wk = wm * amin(ri[p], nb.f[0]);
 #pragma unroll
-                            for (int c = 0; c < NC; ++c) kx[p][c] += wk * sx[c * PL + n];
+                            for (int c = 0; c < NC; ++c) kx[p][c] += wk * nb.f[1 + c];
                             dh[p] += wk;
                         }
                     }
@@ -244,7 +265,7 @@ aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
                     const int64_t oi = cb + c * HW + static_cast<int64_t>(h) * g.W + wcol;
-                    const A xv = sx[c * PL + ci[p]];
+                    const A xv = rec[ci[p]].f[1 + c];
                     const A dhx = dh[p] * xv;
                     Wx[oi] = static_cast<T>((xv - dhx) + kx[p][c]);
                     dhat[oi] = static_cast<T>(dh[p]);
@@ -254,30 +275,35 @@ aggregate_tile(const T* __restrict__ w, const T* __restrict__ x,
     }
 }
 
-// Stages d, r = 1/max(d, eps), image channels, grad_Wx and the per-pixel
-// backward term a(p) = sum_c gdh - gWx x (in channel order).
-template <typename T, int NC, typename A>
+// Stages one record per halo pixel: d, r = 1/max(d, eps), the per-pixel
+// backward term a = sum_c gdh - gWx x (channel order), [g_d,] image
+// channels, grad_Wx.  XO: offset of the image channels (3, or 4 with g_d).
+template <typename T, int NC, int F, int XO, typename A>
 __device__ __forceinline__ void stage_bwd(const Geo& g, const Where& o, int64_t grp,
                                           int64_t cb, int64_t HW, const A* __restrict__ d,
+                                          const A* __restrict__ gd,
                                           const T* __restrict__ x, const T* __restrict__ gWx,
-                                          const T* __restrict__ gdh, A eps, A* sd, A* sr,
-                                          A* sa, A* sx, A* sg) {
-    const int PL = g.XR * g.XP;
+                                          const T* __restrict__ gdh, A eps, Rec<A, F>* rec) {
     const A* dg = d + grp * HW;
     for_halo(g, o.h0, o.w0, [&](int idx, int64_t off) {
+        Rec<A, F> r;
+#pragma unroll
+        for (int k = 0; k < F; ++k) r.f[k] = A(0);
         const A dv = dg[off];
-        sd[idx] = dv;
-        sr[idx] = A(1) / (dv > eps ? dv : eps);
+        r.f[0] = dv;
+        r.f[1] = A(1) / (dv > eps ? dv : eps);
         A a = A(0);
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const A xv = static_cast<A>(to_acc(x[cb + c * HW + off]));
             const A gv = static_cast<A>(to_acc(gWx[cb + c * HW + off]));
-            sx[c * PL + idx] = xv;
-            sg[c * PL + idx] = gv;
+            r.f[XO + c] = xv;
+            r.f[XO + NC + c] = gv;
             a += static_cast<A>(to_acc(gdh[cb + c * HW + off])) - gv * xv;
         }
-        sa[idx] = a;
+        r.f[2] = a;
+        if constexpr (XO == 4) r.f[3] = gd[grp * HW + off];
+        rec[idx] = r;
     });
 }
 
@@ -301,13 +327,10 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
            typename Acc<T>::type* __restrict__ gd, T* __restrict__ gx,
            const ShiftTable st, const Geo g, int use_box, typename Acc<T>::type eps) {
     using A = typename Acc<T>::type;
+    constexpr int F = kBwdAF<A, NC>;
+    constexpr int XO = 3, GO = 3 + NC;
     extern __shared__ __align__(16) unsigned char smem_m[];
-    const int PL = g.XR * g.XP;
-    A* sd = reinterpret_cast<A*>(smem_m);
-    A* sr = sd + PL;
-    A* sa = sr + PL;
-    A* sx = sa + PL;                // [NC]
-    A* sg = sx + NC * PL;           // [NC]
+    Rec<A, F>* rec = reinterpret_cast<Rec<A, F>*>(smem_m);
     const int64_t HW = static_cast<int64_t>(g.H) * g.W;
     const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
     for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
@@ -315,7 +338,8 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
             const Where o = where(g, tile, grp);
             const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
             __syncthreads();
-            stage_bwd<T, NC>(g, o, grp, cb, HW, d, x, gWx, gdh, eps, sd, sr, sa, sx, sg);
+            stage_bwd<T, NC, F, XO>(g, o, grp, cb, HW, d, static_cast<const A*>(nullptr), x,
+                                    gWx, gdh, eps, rec);
             __syncthreads();
             const int wcol = o.w0 + threadIdx.x;
             if (wcol >= g.W) continue;
@@ -327,15 +351,16 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
                 const int h = o.h0 + threadIdx.y + TY * p;
                 hh[p] = h < g.H ? h : g.H - 1;
                 ci[p] = (threadIdx.y + TY * p + g.R) * g.XP + threadIdx.x + g.R;
-                di[p] = sd[ci[p]];
-                ri[p] = sr[ci[p]];
-                aq[p] = sa[ci[p]];
+                const Rec<A, F> me = rec[ci[p]];
+                di[p] = me.f[0];
+                ri[p] = me.f[1];
+                aq[p] = me.f[2];
                 g_d[p] = A(0);
                 const int64_t q = static_cast<int64_t>(hh[p]) * g.W + wcol;
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
-                    xq[p][c] = sx[c * PL + ci[p]];
-                    gq[p][c] = sg[c * PL + ci[p]];
+                    xq[p][c] = me.f[XO + c];
+                    gq[p][c] = me.f[GO + c];
                     gxa[p][c] = gq[p][c] * (A(1) - static_cast<A>(to_acc(dhat[cb + c * HW + q])));
                 }
             }
@@ -356,18 +381,18 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
                         // Pair (q, q + d), weight w_s(q): own forward edge of q
                         // and (inv) the mirror edge of q + d ending at q.
                         if (kp && w_q != A(0)) {
-                            const int n = ci[p] + off;
-                            const A dn = sd[n];
-                            const A r = amin(ri[p], sr[n]);
+                            const Rec<A, F> nb = rec[ci[p] + off];
+                            const A dn = nb.f[0];
+                            const A r = amin(ri[p], nb.f[1]);
                             A Tq = aq[p], Tn = A(0);
 #pragma unroll
-                            for (int c = 0; c < NC; ++c) Tq += gq[p][c] * sx[c * PL + n];
+                            for (int c = 0; c < NC; ++c) Tq += gq[p][c] * nb.f[XO + c];
                             if (inv) {
                                 const A wk = w_q * r;
-                                Tn = sa[n];
+                                Tn = nb.f[2];
 #pragma unroll
                                 for (int c = 0; c < NC; ++c) {
-                                    const A gn = sg[c * PL + n];
+                                    const A gn = nb.f[GO + c];
                                     Tn += gn * xq[p][c];
                                     gxa[p][c] += gn * wk;
                                 }
@@ -378,21 +403,21 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
                         // Pair (q, q - d), weight w_s(q - d): forward edge of
                         // q - d ending at q and (inv) the own mirror edge of q.
                         if (km && w_m != A(0)) {
-                            const int n = ci[p] - off;
-                            const A dn = sd[n];
-                            const A r = amin(ri[p], sr[n]);
+                            const Rec<A, F> nb = rec[ci[p] - off];
+                            const A dn = nb.f[0];
+                            const A r = amin(ri[p], nb.f[1]);
                             const A wk = w_m * r;
-                            A Tn = sa[n], Tq = A(0);
+                            A Tn = nb.f[2], Tq = A(0);
 #pragma unroll
                             for (int c = 0; c < NC; ++c) {
-                                const A gn = sg[c * PL + n];
+                                const A gn = nb.f[GO + c];
                                 Tn += gn * xq[p][c];
                                 gxa[p][c] += gn * wk;
                             }
                             if (inv) {
                                 Tq = aq[p];
 #pragma unroll
-                                for (int c = 0; c < NC; ++c) Tq += gq[p][c] * sx[c * PL + n];
+                                for (int c = 0; c < NC; ++c) Tq += gq[p][c] * nb.f[XO + c];
                             }
                             if ((di[p] > dn ? di[p] : dn) >= eps)
                                 g_d[p] -= (Tn + Tq) * w_m * r * r * share_of(di[p], dn);
@@ -427,14 +452,10 @@ bwd_b_tile(const T* __restrict__ x, const typename Acc<T>::type* __restrict__ d,
            const typename Acc<T>::type* __restrict__ gd, T* __restrict__ gw,
            const ShiftTable st, const Geo g, int use_box, typename Acc<T>::type eps) {
     using A = typename Acc<T>::type;
+    constexpr int F = kBwdBF<A, NC>;
+    constexpr int XO = 4, GO = 4 + NC;
     extern __shared__ __align__(16) unsigned char smem_m[];
-    const int PL = g.XR * g.XP;
-    A* sd = reinterpret_cast<A*>(smem_m);
-    A* sr = sd + PL;
-    A* sa = sr + PL;
-    A* sgd = sa + PL;
-    A* sx = sgd + PL;               // [NC]
-    A* sg = sx + NC * PL;           // [NC]
+    Rec<A, F>* rec = reinterpret_cast<Rec<A, F>*>(smem_m);
     const int64_t HW = static_cast<int64_t>(g.H) * g.W;
     const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
     for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
@@ -442,9 +463,7 @@ bwd_b_tile(const T* __restrict__ x, const typename Acc<T>::type* __restrict__ d,
             const Where o = where(g, tile, grp);
             const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
             __syncthreads();
-            stage_bwd<T, NC>(g, o, grp, cb, HW, d, x, gWx, gdh, eps, sd, sr, sa, sx, sg);
-            const A* gdg = gd + grp * HW;
-            for_halo(g, o.h0, o.w0, [&](int idx, int64_t off) { sgd[idx] = gdg[off]; });
+            stage_bwd<T, NC, F, XO>(g, o, grp, cb, HW, d, gd, x, gWx, gdh, eps, rec);
             __syncthreads();
             const int wcol = o.w0 + threadIdx.x;
             if (wcol >= g.W) continue;
@@ -458,13 +477,14 @@ bwd_b_tile(const T* __restrict__ x, const typename Acc<T>::type* __restrict__ d,
                 act[p] = h < g.H;
                 hh[p] = act[p] ? h : g.H - 1;
                 ci[p] = (threadIdx.y + TY * p + g.R) * g.XP + threadIdx.x + g.R;
-                ri[p] = sr[ci[p]];
-                gdi[p] = sgd[ci[p]];
-                aq[p] = sa[ci[p]];
+                const Rec<A, F> me = rec[ci[p]];
+                ri[p] = me.f[1];
+                aq[p] = me.f[2];
+                gdi[p] = me.f[3];
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
-                    xq[p][c] = sx[c * PL + ci[p]];
-                    gq[p][c] = sg[c * PL + ci[p]];
+                    xq[p][c] = me.f[XO + c];
+                    gq[p][c] = me.f[GO + c];
                 }
             }
             auto body = [&](auto border) {
@@ -478,19 +498,19 @@ bwd_b_tile(const T* __restrict__ x, const typename Acc<T>::type* __restrict__ d,
 #pragma unroll
                     for (int p = 0; p < PPT; ++p) {
                         const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
-                        const int qp = ci[p] + off;
-                        const A r = amin(ri[p], sr[qp]);
+                        const Rec<A, F> nb = rec[ci[p] + off];
+                        const A r = amin(ri[p], nb.f[1]);
                         A v = A(0);
                         if (!use_box || e.in_p) {
                             A G = aq[p];
 #pragma unroll
-                            for (int c = 0; c < NC; ++c) G += gq[p][c] * sx[c * PL + qp];
+                            for (int c = 0; c < NC; ++c) G += gq[p][c] * nb.f[XO + c];
                             v += G * r + gdi[p];
                             if (inv) {
-                                A Gm = sa[qp];
+                                A Gm = nb.f[2];
 #pragma unroll
-                                for (int c = 0; c < NC; ++c) Gm += sg[c * PL + qp] * xq[p][c];
-                                v += Gm * r + sgd[qp];
+                                for (int c = 0; c < NC; ++c) Gm += nb.f[GO + c] * xq[p][c];
+                                v += Gm * r + nb.f[3];
                             }
                         }
                         if (act[p]) gws[e.q] = static_cast<T>(v);
