@@ -10,6 +10,10 @@
  *     allocates device memory and never synchronizes;
  *   - the shift table is a HOST pointer to S rows of `shift_cols` int64
  *     values (dx, dy[, has_inv]); it is copied into the kernel parameters;
+ *     has_inv 0 = no mirror term, 1 = masked mirror (the reference's
+ *     meaning), 2 = periodic mirror (extension, accumulate / normalized:
+ *     the mirror term reads (p - d) mod (H, W) with no inside test; not
+ *     accepted by the row-band entry points);
  *   - inputs keep their storage dtype (fp16/bf16/fp32 are read natively and
  *     promoted in registers; fp64 stays fp64) instead of being copied to a
  *     promoted tensor first;

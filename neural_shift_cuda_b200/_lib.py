@@ -156,12 +156,13 @@ class HostShifts:
     """A contiguous int64 host copy of a shift table, kept alive while the
     ctypes pointer is in use."""
 
-    __slots__ = ("t", "S", "cols")
+    __slots__ = ("t", "S", "cols", "modes")
 
     def __init__(self, t: torch.Tensor):
         self.t = t
         self.S = int(t.shape[0])
         self.cols = int(t.shape[1])
+        self.modes = {}
 
     @property
     def ptr(self):
@@ -169,6 +170,27 @@ class HostShifts:
 
     def rows(self):
         return [tuple(int(v) for v in r) for r in self.t.tolist()]
+
+
+def mirror_mode(hs: HostShifts, periodic: bool) -> HostShifts:
+    """The table as the library reads it: column 2 becomes 0 (no mirror),
+    1 (masked mirror, the reference's meaning of any nonzero value) or, with
+    periodic=True, 2 (periodic mirror) for every row with a mirror term."""
+    if hs.cols != 3:
+        return hs
+    key = bool(periodic)
+    hit = hs.modes.get(key)
+    if hit is not None:
+        return hit
+    col = hs.t[:, 2]
+    if not periodic and bool(((col == 0) | (col == 1)).all()):
+        res = hs
+    else:
+        t = hs.t.clone()
+        t[:, 2] = (col != 0).to(torch.int64) * (2 if periodic else 1)
+        res = HostShifts(t.contiguous())
+    hs.modes[key] = res
+    return res
 
 
 _shift_cache: dict = {}

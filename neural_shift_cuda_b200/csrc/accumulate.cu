@@ -75,8 +75,10 @@ acc_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                 if (i < nc) u[i] += wv * ldg_acc<TX, A>(xb + i * plane_x + xo);
             z += wv;
             if (st.has_inv(s)) {
-                const int64_t hm = h - dx, wm = wcol - dy;
-                if (inb(hm, Hout) && inb(wm, W)) {
+                const bool per = st.has_per(s);   // full-image calls only
+                const int64_t hm = per ? wrap1(h - dx, Hout) : h - dx;
+                const int64_t wm = per ? wrap1(wcol - dy, W) : wcol - dy;
+                if (per || (inb(hm, Hout) && inb(wm, W))) {
                     const A mv = ldg_acc<TW, A>(ws + hm * W + wm);
                     const int64_t mo = xr.own(hm) * W + wm;
 #pragma unroll
@@ -257,9 +259,9 @@ acc_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                     acc[i] += w_src * gU[cb + i * plane + qs];
                     gws += ldg_acc<TX, A>(x + cb + i * plane + qf) * gu_q[i];
                 }
-            if (st.has_inv(s) && inb(h + dx, H) && inb(wcol + dy, W)) {
+            if (st.has_inv(s) && (st.has_per(s) || (inb(h + dx, H) && inb(wcol + dy, W)))) {
                 const A w_q = ldg_acc<TW, A>(ws + q);
-                const int64_t qi = (h + dx) * W + (wcol + dy);
+                const int64_t qi = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
 #pragma unroll
                 for (int i = 0; i < NC; ++i)
                     if (i < nc) {
@@ -486,6 +488,10 @@ static nsc_status band_checks(const char* op, int64_t Hb, int64_t row0,
         return fail(NSC_ERR_INVALID_ARG,
                     "%s: band of %lld rows is thinner than the radius %d", op,
                     (long long)Hb, st.R);
+    if (st.any_per)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: periodic mirror rows (column value 2) are not supported "
+                    "by the row-band split", op);
     return ok();
 }
 

@@ -78,6 +78,7 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     using namespace fast;
     g_decline = "";
     if (std::getenv("NSC_DISABLE_FAST")) DECLINE("disabled by NSC_DISABLE_FAST");
+    if (st.any_per) DECLINE("periodic mirror rows");
     if (xd != wd || (xd != NSC_F16 && xd != NSC_BF16 && xd != NSC_F32)) DECLINE("dtype");
     const int es = xd == NSC_F32 ? 4 : 2;
     const int V = 16 / es;

@@ -108,8 +108,10 @@ norm_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                 seen_invalid = true;
             on.push(kf, xv, logw);
             if (st.has_inv(s)) {
-                const int64_t hm = h - dx, wm = wcol - dy;
-                if (inb(hm, H) && inb(wm, W)) {
+                const bool per = st.has_per(s);
+                const int64_t hm = per ? wrap1(h - dx, H) : h - dx;
+                const int64_t wm = per ? wrap1(wcol - dy, W) : wcol - dy;
+                if (per || (inb(hm, H) && inb(wm, W))) {
                     const int64_t mo = hm * W + wm;
 #pragma unroll
                     for (int i = 0; i < NC; ++i)
@@ -205,8 +207,9 @@ norm_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
             const A vq = ldg_acc<TW, A>(ws + q);
             const A lw_q = as_log(vq, logw);
             const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
-            const bool mir = st.has_inv(s) && inb(h + dx, H) && inb(wcol + dy, W);
-            const int64_t qi = (h + dx) * W + (wcol + dy);
+            const bool mir = st.has_inv(s) &&
+                             (st.has_per(s) || (inb(h + dx, H) && inb(wcol + dy, W)));
+            const int64_t qi = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
             A gws = A(0);
 #pragma unroll
             for (int i = 0; i < NC; ++i) {

@@ -32,8 +32,16 @@ struct ShiftTable {
     int32_t dx[kMaxShifts];
     int32_t dy[kMaxShifts];
     uint32_t inv[kMaxShifts / 32];
+    uint32_t per[kMaxShifts / 32];   // mirror term periodic (column value 2)
+    int32_t any_per;
     __host__ __device__ __forceinline__ bool has_inv(int s) const {
         return (inv[s >> 5] >> (s & 31)) & 1u;
+    }
+    // Periodic mirror: the mirror term reads the weight and x at
+    // (p - d) mod (H, W) with no inside test (an extension of the
+    // reference's row encoding: column value 2).
+    __host__ __device__ __forceinline__ bool has_per(int s) const {
+        return (per[s >> 5] >> (s & 31)) & 1u;
     }
 };
 

@@ -10,8 +10,9 @@ mirror edge that reuses it.
   has_inv flags -- the kernels form the (non-periodic, masked) mirror term
   themselves.
 * comp_box off (periodic): the mirror weight is the forward weight rolled
-  by (dx, dy); it is passed as an explicit (-dx, -dy, 0) row (all mirror
-  rolls in one gather).
+  by (dx, dy) -- the reference materialises those rolled planes as explicit
+  (-dx, -dy, 0) rows; here the same table runs with periodic_mirror=True and
+  the kernels read the mirror weight at (p - d) mod (H, W) directly.
 
 Patched: `forward`, `forward_cached` (cache.shifts / w_fwd_list / comp_box
 / D / C) and `_KT_action(y, guide, sig, return_D, apply_Dinv)`.
@@ -27,7 +28,7 @@ from torch.utils.checkpoint import checkpoint as grad_checkpoint
 
 from ..ops import accumulate_uz, normalized_accumulate_uz, shift_gather
 from ._common import (box_stack, cached_shift_tensor, flat, head_mix_matrix,
-                      mix_heads, normalise_sigma, periodic_edges, shift_tensor)
+                      mix_heads, normalise_sigma, shift_tensor)
 
 
 def _rows(model):
@@ -73,11 +74,12 @@ def _weight_stack(model, x, guide, sig):
 
 
 def _reduction_inputs(model, w, device, H, W, comp_box):
-    """(weights, shifts) for the reduction in either boundary mode."""
+    """(weights, shifts, periodic_mirror) for the reduction in either
+    boundary mode."""
     shifts = _get_shift_tensor(model, device)
     if comp_box:
-        return flat(w * box_stack(shifts[:, :2], H, W, w.dtype, device)), shifts
-    return periodic_edges(w, _rows(model))
+        return flat(w * box_stack(shifts[:, :2], H, W, w.dtype, device)), shifts, False
+    return flat(w), shifts, True
 
 
 def _forward_cuda(self, x, guide=None, sig=None, return_D=True):
@@ -86,10 +88,11 @@ def _forward_cuda(self, x, guide=None, sig=None, return_D=True):
     sig = normalise_sigma(x, sig)
     B, C, H, W = x.shape
     w = _weight_stack(self, x, guide, sig)
-    w_all, shifts = _reduction_inputs(self, w, x.device, H, W,
-                                      bool(getattr(self, "comp_box", True)))
+    w_all, shifts, per = _reduction_inputs(self, w, x.device, H, W,
+                                           bool(getattr(self, "comp_box", True)))
     D, log_Z = normalized_accumulate_uz(x.contiguous(), w_all, shifts,
-                                        return_log_degree=True, validate=False)
+                                        return_log_degree=True, validate=False,
+                                        periodic_mirror=per)
     if not self.training:
         self.max_batch_shifts = None
     return (D, log_Z.exp()) if return_D else (D, None)
@@ -104,11 +107,12 @@ def _kt_action_cuda(self, y, guide=None, sig=None, return_D=False,
     sig = normalise_sigma(y, sig)
     B, C, H, W = y.shape
     w = _weight_stack(self, y, guide, sig)
-    w_all, shifts = _reduction_inputs(self, w, y.device, H, W,
-                                      bool(getattr(self, "comp_box", True)))
-    U, Z = accumulate_uz(y.contiguous(), w_all, shifts)
+    w_all, shifts, per = _reduction_inputs(self, w, y.device, H, W,
+                                           bool(getattr(self, "comp_box", True)))
+    U, Z = accumulate_uz(y.contiguous(), w_all, shifts, periodic_mirror=per)
     if apply_Dinv:
-        U, _ = accumulate_uz((y / Z.clamp_min(1e-6)).contiguous(), w_all, shifts)
+        U, _ = accumulate_uz((y / Z.clamp_min(1e-6)).contiguous(), w_all, shifts,
+                             periodic_mirror=per)
     if not self.training:
         self.max_batch_shifts = None
     return (U, Z) if return_D else (U, None)
@@ -124,7 +128,7 @@ def _pack(self, x, cache):
     key = (tuple(x.shape), x.device, x.dtype)
     st = getattr(self, "_nekde_parallel_weight_cache", None)
     if st is not None and st[0] is cache and st[1] == key:
-        return st[2], st[3]
+        return st[2], st[3], st[4]
     w = list(cache.w_fwd_list)
     if len(w) != len(cache.shifts) or not w:
         raise ValueError("cached w_fwd_list must contain one tensor per cached shift.")
@@ -135,18 +139,16 @@ def _pack(self, x, cache):
             raise ValueError("cached weights and x must share device and dtype.")
     stack = torch.stack(w, 0)
     rows = [(int(dx), int(dy), int(bool(inv))) for dx, dy, inv in cache.shifts]
-    if bool(cache.comp_box):
-        packed = (flat(stack), shift_tensor(rows, x.device))
-    else:
-        packed = periodic_edges(stack, rows)
+    packed = (flat(stack), shift_tensor(rows, x.device), not bool(cache.comp_box))
     self._nekde_parallel_weight_cache = (cache, key, *packed)
     return packed
 
 
 def _forward_cached_cuda(self, x, cache, return_D=True):
-    w_all, shifts = _pack(self, x, cache)
+    w_all, shifts, per = _pack(self, x, cache)
     D, log_Z = normalized_accumulate_uz(x.contiguous(), w_all, shifts,
-                                        return_log_degree=True, validate=False)
+                                        return_log_degree=True, validate=False,
+                                        periodic_mirror=per)
     degree = cache.D if getattr(cache, "D", None) is not None else log_Z.exp()
     return (D, degree) if return_D else (D, None)
 

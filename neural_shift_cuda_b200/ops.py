@@ -252,9 +252,9 @@ class _AccumulateUZFn(torch.autograd.Function):
         return gx.to(x.dtype), gw, None
 
 
-def _prep_reduction(x, weights, shifts, op):
+def _prep_reduction(x, weights, shifts, op, periodic_mirror=False):
     xd, wd = _storage_dtypes(x, weights)
-    hs = _check_shift_shape(shifts, True, op)
+    hs = _lib.mirror_mode(_check_shift_shape(shifts, True, op), periodic_mirror)
     _require_cuda(op, x, weights)
     _check_nchw(x, "x")
     B, C, H, W = x.shape
@@ -264,11 +264,17 @@ def _prep_reduction(x, weights, shifts, op):
     return x.to(xd).contiguous(), w.to(wd), hs
 
 
-def accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts):
+def accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts, *,
+                  periodic_mirror: bool = False):
     """(U_num, Z) over all shifts including the mirror branch of has_inv
     rows; weights are pre-multiplied by the forward box mask by the caller
-    (reference `ops.py:612-631`).  U = U_num / Z is left to the caller."""
-    x_k, w_k, hs = _prep_reduction(x, weights, shifts, "accumulate_uz")
+    (reference `ops.py:612-631`).  U = U_num / Z is left to the caller.
+
+    periodic_mirror=True (an extension): the mirror term of every has_inv
+    row reads w and x at (p - d) mod (H, W) without the inside test -- the
+    periodic (comp_box off) operator, without materialising rolled planes."""
+    x_k, w_k, hs = _prep_reduction(x, weights, shifts, "accumulate_uz",
+                                   periodic_mirror)
     return _AccumulateUZFn.apply(x_k, w_k, hs)
 
 
@@ -327,7 +333,8 @@ class _NormalizedFn(torch.autograd.Function):
 def normalized_accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts,
                              *, log_weights: bool = False,
                              return_log_degree: bool = False,
-                             validate: bool = True):
+                             validate: bool = True,
+                             periodic_mirror: bool = False):
     """Overflow-safe D = K / C over the shift window (reference
     `ops.py:634-679`).
 
@@ -336,9 +343,10 @@ def normalized_accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts,
     return_log_degree=True.  One pass per output with a running maximum;
     empty rows give D = 0, log_C = -inf.  validate=True raises ValueError
     (after the kernel) when a weight is NaN / +inf or a positive weight is
-    negative."""
+    negative.  periodic_mirror=True: mirror terms are periodic (see
+    accumulate_uz)."""
     x_k, w_k, hs = _prep_reduction(x, weights, shifts,
-                                   "normalized_accumulate_uz")
+                                   "normalized_accumulate_uz", periodic_mirror)
     D, L = _NormalizedFn.apply(x_k, w_k, hs, bool(log_weights), bool(validate))
     if return_log_degree:
         return D, L

@@ -161,9 +161,15 @@ def _acc_dtype(*ts):
         else torch.float32
 
 
-def _mirror(w: torch.Tensor, dx: int, dy: int) -> torch.Tensor:
-    """w((h-dx) mod H, (w-dy) mod W) masked by the box of (-dx, -dy)."""
+def _mirror(w: torch.Tensor, dx: int, dy: int, periodic: bool = False) -> torch.Tensor:
+    """w((h-dx) mod H, (w-dy) mod W) masked by the box of (-dx, -dy); with
+    periodic=True unmasked -- the mirror row as the reference patches build
+    it for comp_box off, a forward row over the rolled weight plane
+    (`patches/nekde_drunet_attn_patch.py:346-366`).  Table column value 2
+    selects the periodic form (an extension of the reference's 0/1)."""
     H, W = w.shape[-2:]
+    if periodic:
+        return _gather(w, -dx, -dy)
     return _gather(w, -dx, -dy) * box_mask(H, W, -dx, -dy, w.dtype)
 
 
@@ -186,7 +192,7 @@ def accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts):
         u_terms.append(wf * _gather(x, dx, dy))
         z_terms.append(wf)
         if inv:
-            wi = _mirror(wf, dx, dy)
+            wi = _mirror(wf, dx, dy, inv == 2)
             u_terms.append(wi * _gather(x, -dx, -dy))
             z_terms.append(wi)
     return tree_sum(torch.stack(u_terms)), tree_sum(torch.stack(z_terms))
@@ -215,7 +221,7 @@ def accumulate_uz_backward(x, weights, grad_U, grad_Z, shifts):
         gx = gx + _gather(wf * gU, -dx, -dy)
         gw = _gather(x, dx, dy) * gU + gZ
         if inv:
-            m = box_mask(H, W, dx, dy, dt)
+            m = box_mask(H, W, dx, dy, dt) if inv != 2 else torch.ones(H, W, dtype=dt)
             gx = gx + m * wf * _gather(gU, dx, dy)
             gw = gw + m * (x * _gather(gU, dx, dy) + _gather(gZ, dx, dy))
         if Cw == 1 and C > 1:
@@ -269,7 +275,8 @@ def normalized_accumulate_uz(x, weights, shifts, log_weights=False):
         vals.append(_gather(x, dx, dy))
         if inv:
             wi = _gather(wf, -dx, -dy)
-            keep = box_mask(H, W, -dx, -dy, dt) > 0
+            keep = (box_mask(H, W, -dx, -dy, dt) > 0) if inv != 2 else \
+                torch.ones(H, W, dtype=torch.bool)
             if log_weights:
                 wi = torch.where(keep, wi, torch.full_like(wi, -torch.inf))
             else:
@@ -325,7 +332,8 @@ def normalized_accumulate_uz_backward(x, weights, D, logC, grad_D, grad_logC,
         fac_f = p_f if log_weights else torch.exp(-logC)
         gw = fac_f * score_f
         if inv:
-            m = box_mask(H, W, dx, dy, dt) > 0
+            m = (box_mask(H, W, dx, dy, dt) > 0) if inv != 2 else \
+                torch.ones(H, W, dtype=torch.bool)
             logC_i = _gather(logC, dx, dy)
             p_i = _fraction(lw, logC_i)
             gx = gx + torch.where(m, p_i * _gather(gD, dx, dy),
