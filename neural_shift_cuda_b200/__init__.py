@@ -8,6 +8,7 @@ ABI in `include/nsc_b200.h` (library `_lib/libnsc_b200.so`, built with
 
 from .ops import (
     accumulate_uz,
+    check_validation,
     index_width_bits,
     normalized_accumulate_uz,
     pair_gather,
@@ -23,5 +24,6 @@ __all__ = [
     "accumulate_uz",
     "normalized_accumulate_uz",
     "metropolis_aggregate",
+    "check_validation",
     "index_width_bits",
 ]

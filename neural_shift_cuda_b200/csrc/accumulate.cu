@@ -13,7 +13,7 @@
 // accumulation and adjacent lanes own adjacent pixels, so every weight load
 // of a warp is one coalesced 128-byte row segment.
 //
-// The tiled TMA kernel in accumulate_tma.cu takes over the forward when the
+// The tiled TMA kernel in accumulate_fast.cuh takes over the forward when the
 // geometry allows it; this file is the general path (any W, any alignment).
 
 #include <cstdlib>
@@ -208,8 +208,10 @@ band_add_strips_kernel(A* __restrict__ U, A* __restrict__ Z,
 //   gx(q)   = sum_s w_s(q-d) gU(q-d) [circular] + inv [q+d inside] w_s(q) gU(q+d)
 //   gw_s(q) = sum_c x(q+d) gU(q) + gZ(q) + inv [q+d inside] (x(q) gU(q+d) + gZ(q+d))
 // One pass over the weight stack reads w once (plus the shifted re-read,
-// served by L1/L2) and writes grad_w once.
-template <typename TX, typename TW, int NC>
+// served by L1/L2) and writes grad_w once.  GW == false skips grad_w: a
+// channel-broadcast weight with more than NC channels needs the sum over
+// every channel group, which acc_bwd_gw_bcast_kernel forms instead.
+template <typename TX, typename TW, int NC, bool GW>
 __global__ void __launch_bounds__(kBX * kBY)
 acc_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                const typename Acc<TX>::type* __restrict__ gU,
@@ -270,11 +272,46 @@ acc_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                         gws += xq[i] * g + gZ[cb + i * plane + qi];
                     }
             }
-            gw[wbase + q] = static_cast<TW>(gws);
+            if (GW) gw[wbase + q] = static_cast<TW>(gws);
         }
 #pragma unroll
         for (int i = 0; i < NC; ++i)
             if (i < nc) gx[cb + i * plane + q] = acc[i];
+    }
+}
+
+// grad_w of a channel-broadcast weight (w_channels == 1) for any C: the
+// thread owns pixel q of image b and sums the C channels in a loop, so one
+// thread writes each gw_s(q) exactly once.
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(kBX * kBY)
+acc_bwd_gw_bcast_kernel(const TX* __restrict__ x,
+                        const typename Acc<TX>::type* __restrict__ gU,
+                        const typename Acc<TX>::type* __restrict__ gZ,
+                        TW* __restrict__ gw, const ShiftTable st, int64_t B,
+                        int64_t C, int64_t H, int64_t W) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= H) return;
+    const int64_t plane = H * W;
+    const int64_t q = h * W + wcol;
+    for (int64_t b = blockIdx.z; b < B; b += gridDim.z) {
+        const int64_t cb = b * C * plane;
+        for (int s = 0; s < st.S; ++s) {
+            const int64_t dx = st.dx[s], dy = st.dy[s];
+            const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
+            const bool mir = st.has_inv(s) &&
+                             (st.has_per(s) || (inb(h + dx, H) && inb(wcol + dy, W)));
+            A gws = A(0);
+            for (int64_t c = 0; c < C; ++c) {
+                const int64_t co = cb + c * plane;
+                gws += ldg_acc<TX, A>(x + co + qf) * gU[co + q] + gZ[co + q];
+                if (mir)
+                    gws += ldg_acc<TX, A>(x + co + q) * gU[co + qf] + gZ[co + qf];
+            }
+            gw[(static_cast<int64_t>(s) * B + b) * plane + q] = static_cast<TW>(gws);
+        }
     }
 }
 
@@ -413,12 +450,25 @@ nsc_status acc_bwd(const void* x, int xd, const void* w, int wd, int64_t Cw,
         with_nc(C, Cw, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             const int64_t groups = n_groups(B, C, Cw, NC);
-            acc_bwd_kernel<TX, TW, NC><<<grid_for(W, H, groups), dim3(kBX, kBY),
-                                          0, stream>>>(
-                static_cast<const TX*>(x), static_cast<const TW*>(w),
-                static_cast<const A*>(gU), static_cast<const A*>(gZ),
-                static_cast<A*>(gx), static_cast<TW*>(gw), st, B, C, H, W, Cw,
-                groups);
+            if (Cw == 1 && C > NC) {
+                acc_bwd_kernel<TX, TW, NC, false><<<grid_for(W, H, groups),
+                                                     dim3(kBX, kBY), 0, stream>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<const A*>(gU), static_cast<const A*>(gZ),
+                    static_cast<A*>(gx), static_cast<TW*>(gw), st, B, C, H, W, Cw,
+                    groups);
+                acc_bwd_gw_bcast_kernel<TX, TW><<<grid_for(W, H, B), dim3(kBX, kBY),
+                                                   0, stream>>>(
+                    static_cast<const TX*>(x), static_cast<const A*>(gU),
+                    static_cast<const A*>(gZ), static_cast<TW*>(gw), st, B, C, H, W);
+            } else {
+                acc_bwd_kernel<TX, TW, NC, true><<<grid_for(W, H, groups),
+                                                    dim3(kBX, kBY), 0, stream>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<const A*>(gU), static_cast<const A*>(gZ),
+                    static_cast<A*>(gx), static_cast<TW*>(gw), st, B, C, H, W, Cw,
+                    groups);
+            }
         });
         return check_launch("accumulate_uz_backward");
     });

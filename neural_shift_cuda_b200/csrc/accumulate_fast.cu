@@ -117,7 +117,7 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
         const int Kmax = span <= 4 ? 4 : span <= 8 ? 8 : span <= 12 ? 12 : 16;
         const int XCg = align_up(Kmax, V);
         const size_t plane = static_cast<size_t>(TH + rx) * (TPR * V + XCg) * es;
-        const size_t xt = static_cast<size_t>(NSC_FAST_XBUF) * NC * (TH + 2 * rx) *
+        const size_t xt = NC * (TH + 2 * rx) *
                           (TPR * V + 2 * XCg) * es + 16 + 4 * 16 + 16 + 128;
         while (group_cap > 1 &&
                xt + 3 * (((group_cap * plane + 127) & ~size_t(127)) + 16) > 227u * 1024u)
@@ -213,10 +213,6 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     const int XC = align_up(K, V);
     g.BH = TH + rx;
     g.BW = TW + XC;
-#ifdef NSC_FAST_BOX_PROBE   // throughput probe only (wrong results): smaller boxes
-    if (NSC_FAST_BOX_PROBE & 1) g.BH = TH;
-    if (NSC_FAST_BOX_PROBE & 2) g.BW = TW;
-#endif
     g.stage_tx = static_cast<uint32_t>(g.BH) * g.BW * es;
     g.stage_stride = (g.stage_tx + 127u) & ~127u;
     g.XH = TH + 2 * rx;

@@ -37,23 +37,10 @@
 // reference's pairwise tree (ops.py:77-92).
 #pragma once
 
-// Build-time switch for throughput experiments (0 in every shipped build):
-// 1 = stream the weights without the arithmetic, 2 = arithmetic without
-// waiting for the weights, 3 = as 1 and without staging x, 4 = arithmetic
-// only: no weight copies, no waits, 6 = arithmetic only, static tile order,
-// no barriers at all.
-#ifndef NSC_FAST_EXPERIMENT
-#define NSC_FAST_EXPERIMENT 0
-#endif
 // Up to this many consecutive weight planes (same dx, consecutive plane
 // index, same box origin) travel in one TMA copy.
 #ifndef NSC_FAST_GROUP
 #define NSC_FAST_GROUP 4
-#endif
-// x halo tile buffers: 2 = the next tile's x is prefetched during this one;
-// 1 = one buffer (refilled at the tile boundary), more room for weights
-#ifndef NSC_FAST_XBUF
-#define NSC_FAST_XBUF 1
 #endif
 
 #include "nsc_common.cuh"
@@ -174,17 +161,7 @@ __device__ __forceinline__ void fma_e(float& acc, const uint32_t* w, const uint3
         acc = fmaf(__uint_as_float(w[WI]), __uint_as_float(x[XI]), acc);
     } else {
         const uint32_t ww = w[WI >> 1], xx = x[XI >> 1];
-#ifdef NSC_FAST_FMA_PROBE   // throughput probe only: fp32 FMA on the raw words
-        if constexpr (true) {
-            acc = fmaf(__uint_as_float(ww), __uint_as_float(xx), acc);
-            return;
-        }
-#endif
-#if NSC_FAST_EXPERIMENT == 5
-        constexpr int sel = 0;   // throughput probe only: wrong results
-#else
         constexpr int sel = ((WI & 1) << 1) | (XI & 1);
-#endif
         if constexpr (Elem<T>::kind == 0) {
             if constexpr (sel == 0)
                 asm("{.reg .b16 a0,a1,b0,b1; mov.b32 {a0,a1},%1; mov.b32 {b0,b1},%2; fma.rn.f32.f16 %0, a0, b0, %0;}" : "+f"(acc) : "r"(ww), "r"(xx));
@@ -214,12 +191,6 @@ __device__ __forceinline__ void add_e(float& acc, const uint32_t* w) {
         acc += __uint_as_float(w[WI]);
     } else {
         const uint32_t ww = w[WI >> 1];
-#ifdef NSC_FAST_FMA_PROBE
-        if constexpr (true) {
-            acc += __uint_as_float(ww);
-            return;
-        }
-#endif
         if constexpr (Elem<T>::kind == 0) {
             if constexpr ((WI & 1) == 0)
                 asm("{.reg .b16 a0,a1; mov.b32 {a0,a1},%1; add.f32.f16 %0, a0, %0;}" : "+f"(acc) : "r"(ww));
@@ -377,7 +348,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
     T* xa0 = reinterpret_cast<T*>(smem + NSTAGE * g.stage_stride);
     const int xtile = NC * g.XH * g.XW;
     uint64_t* full = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(xa0 + NSC_FAST_XBUF * xtile) + 15) & ~uintptr_t(15));
+        (reinterpret_cast<uintptr_t>(xa0 + xtile) + 15) & ~uintptr_t(15));
     uint64_t* empty = full + NSTAGE;
     // Dynamic tile order: the producer draws tickets from a global counter
     // (two tiles ahead) and publishes them in a 4-slot ring.  Tiles are then
@@ -405,7 +376,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
 
     // ------------------------------------------------------------ producer
     if (tid >= NCONS) {
-        if (tid != NCONS || NSC_FAST_EXPERIMENT == 6) return;
+        if (tid != NCONS) return;
         uint32_t it = 0;
         int stage = 0;
         uint32_t phase = 0;
@@ -439,12 +410,6 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                         *(volatile int*)&abort_flag = 1;
                         break;
                     }
-                    if (NSC_FAST_EXPERIMENT == 4) {   // handshake without a copy
-                        mbar_arrive(&full[stage]);
-                        ++it;
-                        if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-                        continue;
-                    }
                     mbar_arrive_expect_tx(&full[stage], len * g.plane_bytes);
                     const int mo = dy > 0 ? align_up(dy, V) : 0;
                     // weight plane (s, b, wc) is slice s of the (B*Cw) index
@@ -462,8 +427,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         }
         // Drain: the CTA must not exit with copies into its shared memory in
         // flight.  Wait (bounded) for the last NSTAGE loads to land.
-        const uint32_t n = NSC_FAST_EXPERIMENT == 4 ? 0u
-                           : (it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE);
+        const uint32_t n = it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE;
         for (uint32_t j = it - n; j < it; ++j)
             mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts);
         return;
@@ -519,29 +483,24 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
 
     // Tile k of this CTA (ring slot k & 3), -1 when the schedule is done.
     auto tile_at = [&](uint32_t k) -> int64_t {
-        if (NSC_FAST_EXPERIMENT == 6) {
-            const int64_t t = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
-            return t < g.ntiles ? t : -1;
-        }
         if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts)) {
             dead = true;
             *(volatile int*)&abort_flag = 1;
         }
         return dead ? -1 : *(volatile int64_t*)&tile_ring[k & 3];
     };
-    int buf = 0;
     int64_t tile = tile_at(0);
-    if (NSC_FAST_EXPERIMENT != 3 && tile >= 0) issue_x(tile, xa0);
+    if (tile >= 0) issue_x(tile, xa0);
     for (uint32_t k = 0; tile >= 0; ++k) {
         const TileId id = decode_tile(tile, g, TW, cgroups);
         const int64_t b = id.b;
         const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
         const int h0 = id.h0, w0 = id.w0;
-        if (NSC_FAST_XBUF == 1 && k > 0) {
+        if (k > 0) {
             named_sync(1, NCONS);   // every thread is done with the previous tile
-            if (NSC_FAST_EXPERIMENT != 3) issue_x(tile, xa0);
+            issue_x(tile, xa0);
         }
-        T* xa = xa0 + buf * xtile;
+        T* xa = xa0;
         const bool row_border = h0 - Rx < 0 || h0 + TH + Rx > g.H;
         const bool col_border = w0 - XC < 0 || w0 + TW + XC + V > g.W;
 
@@ -550,7 +509,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         cp_async_wait_all();
         named_sync(1, NCONS);
         if (*(volatile int*)&abort_flag) break;
-        if (NSC_FAST_EXPERIMENT != 3 && (row_border || col_border)) {
+        if (row_border || col_border) {
             for (int idx = tid; idx < xtotal; idx += NCONS) {
                 int c, i, jv;
                 int64_t r, col0, xr;
@@ -567,10 +526,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
             }
             named_sync(1, NCONS);
         }
-        // prefetch the next tile's x while this one computes
         const int64_t next = tile_at(k + 1);
-        if (NSC_FAST_XBUF == 2 && NSC_FAST_EXPERIMENT != 3 && next >= 0)
-            issue_x(next, xa0 + (buf ^ 1) * xtile);
 
         float u[NC][V], z[V];
 #pragma unroll
@@ -624,25 +580,21 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
             // entry waits for it); last: the copy is released afterwards
             auto one = [&](auto dyc, const int pos, const bool last, const bool inv) {
                 constexpr int dy = decltype(dyc)::value;
-                if (NSC_FAST_EXPERIMENT != 2 && NSC_FAST_EXPERIMENT != 6 && pos == 0)
+                if (pos == 0)
                     mbar_wait32_ab(full32 + 8 * stage, phase, timeouts,
                                    (volatile int*)&abort_flag);
                 const uint32_t sp = after(stp) + pos * g.plane_bytes;
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
                 lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
-                if constexpr (NSC_FAST_EXPERIMENT == 1 || NSC_FAST_EXPERIMENT == 3) {
-                    z[0] += __uint_as_float(wv[0] ^ wv[1] ^ wv[2] ^ wv[3]);
-                } else {
-                    static_for<0, V>([&](auto ic) {
-                        constexpr int i = decltype(ic)::value;
+                static_for<0, V>([&](auto ic) {
+                    constexpr int i = decltype(ic)::value;
 #pragma unroll
-                        for (int c = 0; c < NC; ++c)
-                            fma_e<T, i, XC + dy + i - FWL * EPW>(u[c][i], wv, xf[c]);
-                        add_e<T, i>(z[i], wv);
-                    });
-                }
-                if (NSC_FAST_EXPERIMENT != 1 && NSC_FAST_EXPERIMENT != 3 && inv) {
+                    for (int c = 0; c < NC; ++c)
+                        fma_e<T, i, XC + dy + i - FWL * EPW>(u[c][i], wv, xf[c]);
+                    add_e<T, i>(z[i], wv);
+                });
+                if (inv) {
                     constexpr int moff = mo - dy;               // >= 0
                     constexpr int kk = moff % V;
                     constexpr int mb = moff - kk;
@@ -660,7 +612,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 }
                 if (last) {   // copy fully used: release it
                     __syncwarp();
-                    if (lane == 0 && NSC_FAST_EXPERIMENT != 6) mbar_arrive32(empty32 + 8 * stage);
+                    if (lane == 0) mbar_arrive32(empty32 + 8 * stage);
                     if (++stage == NSTAGE) {
                         stage = 0;
                         phase ^= 1u;
@@ -710,7 +662,6 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 }
             }
         }
-        if (NSC_FAST_XBUF == 2) buf ^= 1;
         tile = next;
     }
     cp_async_wait_all();

@@ -25,7 +25,7 @@ bool launch(const WMaps& maps, const void* x, void* U, void* Z,
     }
     // ring depth: as many weight stages (<= 12) as fit next to the two
     // x tiles in the 227 KB a CTA may use
-    const size_t fixed = static_cast<size_t>(NSC_FAST_XBUF) * NC * g.XH * g.XW * sizeof(T) +
+    const size_t fixed = NC * g.XH * g.XW * sizeof(T) +
                          16 + 4 * 16 + 16 + 128;
     const size_t per_stage = g.stage_stride + 2 * sizeof(uint64_t);
     const size_t cap = 227u * 1024u;

@@ -163,7 +163,10 @@ __device__ __forceinline__ A fraction(A lw, A lc) {
 //   gw_s(q) = fac(q) (gD(q) (x(q+d) - D(q)) + gL(q))
 //           + inv [q+d inside] fac'(q+d) (gD(q+d) (x(q) - D(q+d)) + gL(q+d))
 // with fac = p (log mode) or exp(-logC) (positive mode); gw = 0 for masked.
-template <typename TX, typename TW, int NC>
+// GW == false skips grad_w: a channel-broadcast weight with more than NC
+// channels needs the sum over every channel group, which
+// norm_bwd_gw_bcast_kernel forms instead.
+template <typename TX, typename TW, int NC, bool GW>
 __global__ void __launch_bounds__(kBX * kBY)
 norm_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                 const typename Acc<TX>::type* __restrict__ D,
@@ -227,11 +230,58 @@ norm_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                 }
             }
             if (lw_q == neg_inf<A>()) gws = A(0);
-            gw[wbase + q] = static_cast<TW>(gws);
+            if (GW) gw[wbase + q] = static_cast<TW>(gws);
         }
 #pragma unroll
         for (int i = 0; i < NC; ++i)
             if (i < nc) gx[cb + i * plane + q] = acc[i];
+    }
+}
+
+// grad_w of a channel-broadcast weight (w_channels == 1) for any C: the
+// thread owns pixel q of image b and sums the C channels in a loop, so one
+// thread writes each gw_s(q) exactly once.
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(kBX * kBY)
+norm_bwd_gw_bcast_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                         const typename Acc<TX>::type* __restrict__ D,
+                         const typename Acc<TX>::type* __restrict__ L,
+                         const typename Acc<TX>::type* __restrict__ gD,
+                         const typename Acc<TX>::type* __restrict__ gL,
+                         TW* __restrict__ gw, const ShiftTable st, int64_t B,
+                         int64_t C, int64_t H, int64_t W, int logw) {
+    using A = typename Acc<TX>::type;
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= H) return;
+    const int64_t plane = H * W;
+    const int64_t q = h * W + wcol;
+    for (int64_t b = blockIdx.z; b < B; b += gridDim.z) {
+        const int64_t cb = b * C * plane;
+        for (int s = 0; s < st.S; ++s) {
+            const int64_t dx = st.dx[s], dy = st.dy[s];
+            const int64_t wq = (static_cast<int64_t>(s) * B + b) * plane + q;
+            const A lw_q = as_log(ldg_acc<TW, A>(w + wq), logw);
+            const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
+            const bool mir = st.has_inv(s) &&
+                             (st.has_per(s) || (inb(h + dx, H) && inb(wcol + dy, W)));
+            A gws = A(0);
+            for (int64_t c = 0; c < C; ++c) {
+                const int64_t co = cb + c * plane;
+                const A Lq = L[co + q];
+                const A score = gD[co + q] * (ldg_acc<TX, A>(x + co + qf) - D[co + q]) +
+                                gL[co + q];
+                gws += (logw ? fraction(lw_q, Lq) : exp_acc(-Lq)) * score;
+                if (mir) {
+                    const A Li = L[co + qf];
+                    const A score_i =
+                        gD[co + qf] * (ldg_acc<TX, A>(x + co + q) - D[co + qf]) + gL[co + qf];
+                    gws += (logw ? fraction(lw_q, Li) : exp_acc(-Li)) * score_i;
+                }
+            }
+            if (lw_q == neg_inf<A>()) gws = A(0);
+            gw[wq] = static_cast<TW>(gws);
+        }
     }
 }
 
@@ -351,13 +401,26 @@ nsc_status nsc_normalized_accumulate_uz_bwd(
         with_nc(C, w_channels, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             const int64_t groups = n_groups(B, C, w_channels, NC);
-            norm_bwd_kernel<TX, TW, NC><<<grid_for(W, H, groups),
-                                           dim3(kBX, kBY), 0, sm>>>(
-                static_cast<const TX*>(x), static_cast<const TW*>(w),
-                static_cast<const A*>(D), static_cast<const A*>(log_C),
-                static_cast<const A*>(grad_D), static_cast<const A*>(grad_log_C),
-                static_cast<A*>(grad_x), static_cast<TW*>(grad_w), st, B, C, H,
-                W, w_channels, log_weights ? 1 : 0, groups);
+            const bool split = w_channels == 1 && C > NC;
+            auto launch = [&](auto kern) {
+                kern<<<grid_for(W, H, groups), dim3(kBX, kBY), 0, sm>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<const A*>(D), static_cast<const A*>(log_C),
+                    static_cast<const A*>(grad_D), static_cast<const A*>(grad_log_C),
+                    static_cast<A*>(grad_x), static_cast<TW*>(grad_w), st, B, C, H,
+                    W, w_channels, log_weights ? 1 : 0, groups);
+            };
+            if (split) {
+                launch(norm_bwd_kernel<TX, TW, NC, false>);
+                norm_bwd_gw_bcast_kernel<TX, TW><<<grid_for(W, H, B), dim3(kBX, kBY),
+                                                    0, sm>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<const A*>(D), static_cast<const A*>(log_C),
+                    static_cast<const A*>(grad_D), static_cast<const A*>(grad_log_C),
+                    static_cast<TW*>(grad_w), st, B, C, H, W, log_weights ? 1 : 0);
+            } else {
+                launch(norm_bwd_kernel<TX, TW, NC, true>);
+            }
         });
         return check_launch(op);
     });

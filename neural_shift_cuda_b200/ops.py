@@ -18,20 +18,24 @@ reference (`neural_shift_cuda/ops.py:576-679`).  Every op is a
 * A weight stack may be channel-broadcast: `(S*B, 1, H, W)` with C > 1, or
   a stride-0 `expand` of it.  It is read once per pixel for all channels.
 * `validate=True` in `normalized_accumulate_uz` is checked inside the
-  reduction kernel (no extra pass over the weights); a violation raises
-  ValueError after the kernel completes.
+  reduction kernel (no extra pass over the weights) and, like the
+  reference's `torch._assert_async`, without a host synchronisation: the
+  kernel's flag word is copied to pinned host memory behind an event and a
+  violation raises ValueError at the next normalized call or backward that
+  finds the copy complete, or at `check_validation()`, which waits for it.
 """
 
 from __future__ import annotations
 
-from typing import Tuple
+import threading
+from typing import List, Tuple
 
 import torch
 
 from . import _lib
 
 __all__ = ["shift_gather", "pair_gather", "accumulate_uz",
-           "normalized_accumulate_uz", "index_width_bits"]
+           "normalized_accumulate_uz", "check_validation", "index_width_bits"]
 
 _MAX_S = 1024
 
@@ -285,6 +289,46 @@ def accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts, *,
 _POS_MSG = "positive weights must be finite and nonnegative"
 _LOG_MSG = "log_weights may be finite or -inf (mask), but not NaN or +inf"
 
+# Validation flags of launched normalized forwards whose result the host has
+# not read yet: (pinned host copy, event after the copy, log_weights).
+_pending: List[Tuple[torch.Tensor, "torch.cuda.Event", bool]] = []
+_pending_lock = threading.Lock()
+
+
+def _defer_flag(flag: torch.Tensor, log_weights: bool) -> None:
+    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    host.copy_(flag, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(flag.device))
+    with _pending_lock:
+        _pending.append((host, ev, bool(log_weights)))
+
+
+def check_validation(block: bool = True) -> None:
+    """Raise ValueError if a `validate=True` normalized forward launched so
+    far saw a NaN / +inf weight (or a negative positive-mode weight).
+
+    block=True waits for the pending flag copies (a host synchronisation on
+    their streams); block=False only reads the copies that have completed.
+    Each flag is reported once."""
+    with _pending_lock:
+        todo = list(_pending)
+        _pending.clear()
+    keep, bad = [], None
+    for host, ev, lw in todo:
+        if block:
+            ev.synchronize()
+        elif not ev.query():
+            keep.append((host, ev, lw))
+            continue
+        if bad is None and int(host[0]) != 0:
+            bad = lw
+    if keep:
+        with _pending_lock:
+            _pending[:0] = keep
+    if bad is not None:
+        raise ValueError(_LOG_MSG if bad else _POS_MSG)
+
 
 class _NormalizedFn(torch.autograd.Function):
     @staticmethod
@@ -301,8 +345,8 @@ class _NormalizedFn(torch.autograd.Function):
                       _lib.dtype_code(w.dtype), w.size(1), B, C, H, W,
                       hs.ptr, hs.S, int(bool(log_weights)), _lib.ptr(D),
                       _lib.ptr(L), _lib.ptr(flag), _lib.stream_of(x))
-        if flag is not None and int(flag.item()) != 0:
-            raise ValueError(_LOG_MSG if log_weights else _POS_MSG)
+        if flag is not None:
+            _defer_flag(flag, log_weights)
         ctx.save_for_backward(x, w, D, L)
         ctx.hs = hs
         ctx.log_weights = bool(log_weights)
@@ -311,6 +355,7 @@ class _NormalizedFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_D, grad_L):
+        check_validation(block=False)
         x, w, D, L = ctx.saved_tensors
         hs = ctx.hs
         B, C, H, W = x.shape
@@ -341,10 +386,12 @@ def normalized_accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts,
     weights: (S*B, C, H, W) positive weights (0 masks) or, with
     log_weights=True, logits (-inf masks).  Returns D, or (D, log_C) with
     return_log_degree=True.  One pass per output with a running maximum;
-    empty rows give D = 0, log_C = -inf.  validate=True raises ValueError
-    (after the kernel) when a weight is NaN / +inf or a positive weight is
-    negative.  periodic_mirror=True: mirror terms are periodic (see
-    accumulate_uz)."""
+    empty rows give D = 0, log_C = -inf.  validate=True flags a NaN / +inf
+    weight or a negative positive-mode weight on the device; the ValueError
+    is raised without a host synchronisation by a later normalized call or
+    backward, or at once by `check_validation()`.  periodic_mirror=True:
+    mirror terms are periodic (see accumulate_uz)."""
+    check_validation(block=False)
     x_k, w_k, hs = _prep_reduction(x, weights, shifts,
                                    "normalized_accumulate_uz", periodic_mirror)
     D, L = _NormalizedFn.apply(x_k, w_k, hs, bool(log_weights), bool(validate))

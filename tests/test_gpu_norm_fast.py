@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(autouse=True)
-def _require_fast(monkeypatch):
+def _require_fast(monkeypatch, cuda):
     monkeypatch.setenv("NSC_REQUIRE_FAST", "1")
 
 
@@ -32,6 +32,8 @@ def T(rows):
 def run(x, k, sh, logw, validate=False):
     D, L = nsc.normalized_accumulate_uz(x.cuda(), k.cuda(), sh, log_weights=logw,
                                         return_log_degree=True, validate=validate)
+    if validate:
+        nsc.check_validation()
     return D.cpu(), L.cpu()
 
 

@@ -215,6 +215,32 @@ def test_accumulate_backward_broadcast(cuda):
     close(wc.grad, gw, 1e-10, 1e-10)
 
 
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-10),
+                                       (torch.float32, 1e-4)])
+@pytest.mark.parametrize("C", [5, 8])
+@pytest.mark.parametrize("expand", [False, True])
+def test_accumulate_backward_broadcast_many_channels(cuda, C, dtype, tol, expand):
+    """A channel-shared weight with more channels than one thread's channel
+    tile: grad_w is the sum over all C channels, written once per element."""
+    torch.manual_seed(11)
+    B, H, W = 2, 13, 11
+    sh = T(O.halfplane_shifts(2))
+    x = torch.randn(B, C, H, W, dtype=torch.float64)
+    w = O.premasked_weights(torch.rand(len(sh) * B, 1, H, W,
+                                       dtype=torch.float64), sh, B)
+    xc = x.to(dtype).to(cuda).requires_grad_(True)
+    wc = w.to(dtype).to(cuda).requires_grad_(True)
+    U, Z = nsc.accumulate_uz(xc, wc.expand(-1, C, -1, -1) if expand else wc, sh)
+    Ur, Zr = O.accumulate_uz(x, w, sh)
+    close(U, Ur, tol, tol)
+    close(Z, Zr, tol, tol)
+    gU, gZ = torch.randn_like(x), torch.randn_like(x)
+    (U * gU.to(dtype).to(cuda) + Z * gZ.to(dtype).to(cuda)).sum().backward()
+    gx, gw = O.accumulate_uz_backward(x, w, gU, gZ, sh)
+    close(xc.grad, gx, tol, tol)
+    close(wc.grad, gw, tol, tol)
+
+
 @pytest.mark.parametrize("R", [1, 2])
 def test_accumulate_gradcheck(cuda, R):
     torch.manual_seed(0)
@@ -319,6 +345,37 @@ def test_normalized_fp64_and_grads(cuda, log_weights, table):
     close(wc.grad, gw, 1e-9, 1e-9)
 
 
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-9),
+                                       (torch.float32, 1e-4)])
+@pytest.mark.parametrize("C", [5, 8])
+@pytest.mark.parametrize("log_weights", [False, True])
+@pytest.mark.parametrize("expand", [False, True])
+def test_normalized_backward_broadcast_many_channels(cuda, C, log_weights, dtype,
+                                                     tol, expand):
+    """normalized_accumulate_uz with channel-shared weights and C > 4:
+    grad_w sums every channel's contribution."""
+    torch.manual_seed(12)
+    B, H, W = 2, 9, 10
+    sh = T(O.halfplane_shifts(2))
+    x = torch.randn(B, C, H, W, dtype=torch.float64)
+    raw = torch.randn(len(sh) * B, 1, H, W, dtype=torch.float64)
+    w = raw if log_weights else raw.exp()
+    xc = x.to(dtype).to(cuda).requires_grad_(True)
+    wc = w.to(dtype).to(cuda).requires_grad_(True)
+    D, L = nsc.normalized_accumulate_uz(
+        xc, wc.expand(-1, C, -1, -1) if expand else wc, sh,
+        log_weights=log_weights, return_log_degree=True)
+    Dr, Lr = O.normalized_accumulate_uz(x, w, sh, log_weights)
+    close(D, Dr, tol, tol)
+    close(L, Lr, tol, tol)
+    gD, gL = torch.randn_like(x), torch.randn_like(x)
+    (D * gD.to(dtype).to(cuda) + L * gL.to(dtype).to(cuda)).sum().backward()
+    gx, gw = O.normalized_accumulate_uz_backward(x, w, Dr, Lr, gD, gL, sh,
+                                                 log_weights)
+    close(xc.grad, gx, tol, tol)
+    close(wc.grad, gw, tol, tol)
+
+
 @pytest.mark.parametrize("log_weights", [False, True])
 def test_normalized_gradcheck(cuda, log_weights):
     torch.manual_seed(2)
@@ -384,9 +441,15 @@ def test_normalized_special_values(cuda):
     assert math.isnan(D[0, 0, 2, 2]) and math.isnan(L[0, 0, 2, 2])
     with pytest.raises(ValueError, match=r"not NaN or \+inf"):
         nsc.normalized_accumulate_uz(x.cuda(), lw.cuda(), sh, log_weights=True)
+        nsc.check_validation()
     with pytest.raises(ValueError, match="nonnegative"):
         nsc.normalized_accumulate_uz(x.cuda(), -lw.abs().nan_to_num(1.0).cuda(),
                                      sh)
+        nsc.check_validation()
+    # valid weights leave nothing pending
+    nsc.normalized_accumulate_uz(x.cuda(), lw.nan_to_num(0.0, posinf=0.0).cuda(),
+                                 sh, log_weights=True)
+    nsc.check_validation()
 
 
 def test_normalized_offset_invariance(cuda):
