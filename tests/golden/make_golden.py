@@ -197,8 +197,60 @@ def main(ref_root):
                           Z_serial=Z_ser, U_patched=U_p, Z_patched=Z_p,
                           args=vars(args))
     torch.save(nectr, os.path.join(HERE, "golden_nectr.pt"))
-    print("wrote", sorted(cases), sorted(nectr))
+    inst = installer_cases()
+    torch.save(inst, os.path.join(HERE, "golden_installers.pt"))
+    print("wrote", sorted(cases), sorted(nectr), sorted(inst))
+
+
+def installer_cases():
+    """The reference's own GASD / NeKDe / NKD_mp installer functions on the
+    stub models of tests/stub_models.py, on the CPU (where the reference
+    ops run their PyTorch paths), fp64."""
+    sys.path.insert(0, os.path.dirname(HERE))
+    import stub_models as SM
+    from neural_shift_cuda.integration import gasd_drunet_attn_patch as rg
+    from neural_shift_cuda.integration import nekde_drunet_attn_patch as rn
+    from neural_shift_cuda.integration import nkd_metropolis_attn_patch as rm
+    mods = {"gasd": rg, "nekde": rn, "nkd": rm}
+    out = {}
+    for case in SM.INSTALLER_CASES:
+        kind, B, C, H, W, R, heads, box, seed = case
+        cls = SM.make_class(kind)
+        mods[kind].install_cuda_shift(cls)
+        m = SM.make_model(kind, C, R, heads, box, seed, cls=cls)
+        g = torch.Generator().manual_seed(seed)
+        x = torch.rand(B, C, H, W, generator=g, dtype=torch.float64)
+        y = torch.randn(B, C, H, W, generator=g, dtype=torch.float64)
+        guide = torch.rand(B, C, H, W, generator=g, dtype=torch.float64)
+        rec = dict(case=case, state=m.state_dict(), x=x, y=y, guide=guide)
+        with torch.no_grad():
+            if kind == "gasd":
+                rec["D"], rec["Z"] = rg._forward_cuda(m, x)
+                rec["D_guided"], _ = rg._forward_cuda(m, x, guide=guide)
+                rec["KT"] = rg._kt_action_cuda(m, y, guide=guide)
+                rec["WT"], rec["WT_D"] = rg._nlm_transpose_cuda(
+                    m, x, guide=guide, return_D=True)
+                rec["LAP"] = rg._laplacian_grw_cuda(m, x, guide)
+            elif kind == "nekde":
+                rec["D"], rec["Z"] = rn._forward_cuda(m, x)
+                rec["D_guided"], _ = rn._forward_cuda(m, x, guide=guide)
+                rec["KT"], rec["KT_Z"] = rn._kt_action_cuda(
+                    m, y, guide=guide, return_D=True)
+                rec["KTD"], _ = rn._kt_action_cuda(
+                    m, y, guide=guide, return_D=True, apply_Dinv=True)
+            else:
+                rec["Wx"], rec["d_hat"] = rm._forward_cuda(m, x, return_D=True)
+                rec["Wx_guided"], _ = rm._forward_cuda(m, x, guide=guide)
+        out[SM.case_name(case)] = rec
+    return out
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ["NSC_REFERENCE"])
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ["NSC_REFERENCE"]
+    if "--installers-only" in sys.argv:
+        sys.path.insert(0, root)
+        inst = installer_cases()
+        torch.save(inst, os.path.join(HERE, "golden_installers.pt"))
+        print("wrote", sorted(inst))
+    else:
+        main(root)

@@ -4,12 +4,14 @@
   the installed CUDA forward, against the reference's serial and patched
   outputs (fp64).
 * GASD / NeKDe / NKD_mp: the model files are not part of the reference
-  checkout, so small stub models implement exactly the attributes the
-  installers call (`pre_activation`, `_collect_shifts`, the per-shift
-  weight producers, head mixing); the installed forwards are checked
-  against direct CPU restatements of the operators they implement (the
-  reference's own cached-path tests use the same approach,
-  tests/test_cached_forward_patches.py).
+  checkout, so small stub models (tests/stub_models.py) implement exactly
+  the attributes the installers call (`pre_activation`, `_collect_shifts`,
+  the per-shift weight producers, head mixing).  The installed forwards,
+  K^T actions, NLM transpose and Laplacian are checked against the
+  reference's own installer functions run on the same stubs on the CPU
+  (tests/golden/golden_installers.pt), and against direct CPU restatements
+  of the operators they implement (the reference's own cached-path tests
+  use the same approach, tests/test_cached_forward_patches.py).
 """
 
 import os
@@ -23,11 +25,16 @@ import torch.nn.functional as F
 from neural_shift_cuda_b200 import integration as I
 from oracle import nsc_oracle as O
 from oracle.nectr_model import NECTR_denoiser
+import stub_models as SM
 
 pytestmark = pytest.mark.gpu
 
 GOLD_NECTR = torch.load(os.path.join(os.path.dirname(__file__), "golden",
                                      "golden_nectr.pt"), weights_only=False)
+GOLD_INST = torch.load(os.path.join(os.path.dirname(__file__), "golden",
+                                    "golden_installers.pt"), weights_only=False)
+_INSTALL = {"gasd": I.install_cuda_shift_gasd, "nekde": I.install_cuda_shift_attn,
+            "nkd": I.install_cuda_shift_metropolis}
 
 
 def _roll(x, dx, dy):
@@ -88,52 +95,7 @@ def test_nectr_fp32_and_bf16_inputs(cuda):
 
 # ------------------------------------------------------------ stub models
 
-class _StubBase(nn.Module):
-    """The model contract the attention installers use."""
-
-    def __init__(self, C, R, heads, comp_box, table):
-        super().__init__()
-        self.window_rad = R
-        self.comp_box = comp_box
-        self.max_batch_shifts = None
-        self.output_activation = "softmax"
-        self.raw_head_mix = (nn.Parameter(torch.randn(C, heads))
-                             if heads not in (1, C) else None)
-        self.feat = nn.Conv2d(C, 4, 3, padding=1)
-        self.score = nn.Conv2d(8, heads, 1)
-        self._table = table
-        self._gather_core = True
-
-    def pre_activation(self, x, sigma=None):
-        return torch.tanh(self.feat(x))
-
-    def _collect_shifts(self):
-        return list(self._table)
-
-    def _weights(self, phi, shifts):
-        logits = torch.stack([self.score(torch.cat([phi, _roll(phi, s[0], s[1])], 1))
-                              for s in shifts], 0)
-        return list(F.softmax(logits, dim=0))          # (B, heads, H, W) each
-
-    def _all_shift_weights(self, phi, padded_phi, sig, shifts):
-        return self._weights(phi, shifts)
-
-    def _halfplane_weights(self, phi, padded_phi, sig, shifts):
-        return self._weights(phi, shifts)
-
-    def _head_mix_matrix(self):
-        return (F.softmax(self.raw_head_mix, dim=1)
-                if self.raw_head_mix is not None else None)
-
-    def _mix_heads(self, w, C, mat):
-        if w.shape[1] == 1:
-            return w.expand(-1, C, -1, -1)
-        if mat is not None:
-            return torch.einsum("ch,bhij->bcij", mat, w)
-        return w
-
-    def _normalise_sigma(self, x, sig):
-        return sig
+_StubBase = SM.StubBase
 
 
 def _mixed(m, x):
@@ -268,3 +230,50 @@ def test_cached_forwards(cuda, use_box):
     torch.testing.assert_close(out.cpu(), Kx / Zg, rtol=1e-10, atol=1e-10)
     torch.testing.assert_close(gp._kt_action_cached_cuda(model, x, cache).cpu(), KT,
                                rtol=1e-10, atol=1e-10)
+
+
+# ------------------------------------------- pinned to the reference installers
+
+def _close(a, b):
+    torch.testing.assert_close(a.detach().cpu().to(b.dtype), b, rtol=1e-10,
+                               atol=1e-10)
+
+
+@pytest.mark.parametrize("name", sorted(GOLD_INST))
+def test_installers_match_reference_installers(cuda, name):
+    """This package's installed methods on a stub model vs the reference's
+    installer functions on the same stub and weights (fp64)."""
+    c = GOLD_INST[name]
+    kind, B, C, H, W, R, heads, box, seed = c["case"]
+    cls = SM.make_class(kind, f"Pinned_{name}")
+    _INSTALL[kind](cls)
+    m = SM.make_model(kind, C, R, heads, box, seed, cls=cls)
+    m.load_state_dict(c["state"])
+    m = m.to(cuda)
+    x, y, guide = (c[k].to(cuda) for k in ("x", "y", "guide"))
+    with torch.no_grad():
+        if kind == "gasd":
+            D, Z = m(x)
+            _close(D, c["D"])
+            _close(Z, c["Z"])
+            _close(m(x, guide=guide)[0], c["D_guided"])
+            _close(m._KT_action(y, guide=guide), c["KT"])
+            WT, WTD = m.NLM_transpose(x, guide=guide, return_D=True)
+            _close(WT, c["WT"])
+            _close(WTD, c["WT_D"])
+            _close(m.laplacian_grw(x, guide), c["LAP"])
+        elif kind == "nekde":
+            D, Z = m(x)
+            _close(D, c["D"])
+            _close(Z, c["Z"])
+            _close(m(x, guide=guide)[0], c["D_guided"])
+            KT, KZ = m._KT_action(y, guide=guide, return_D=True)
+            _close(KT, c["KT"])
+            _close(KZ, c["KT_Z"])
+            KTD, _ = m._KT_action(y, guide=guide, return_D=True, apply_Dinv=True)
+            _close(KTD, c["KTD"])
+        else:
+            Wx, dh = m(x, return_D=True)
+            _close(Wx, c["Wx"])
+            _close(dh, c["d_hat"])
+            _close(m(x, guide=guide)[0], c["Wx_guided"])

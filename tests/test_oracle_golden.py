@@ -114,3 +114,49 @@ def test_nectr_model_restatement(act):
         U, Z = m(c["x"])
     _close(U, c["U_serial"], 1e-12, 1e-12)
     _close(Z, c["Z_serial"], 1e-12, 1e-12)
+
+
+# ---------------------------------------------------------------------------
+# installers: the oracle's operators on the stub models' weights against the
+# reference's own installer functions (tests/golden/golden_installers.pt)
+# ---------------------------------------------------------------------------
+
+GOLD_INST = torch.load(os.path.join(os.path.dirname(__file__), "golden",
+                                    "golden_installers.pt"), weights_only=False)
+
+
+@pytest.mark.parametrize("name", sorted(GOLD_INST))
+def test_oracle_matches_reference_installers(name):
+    import stub_models as SM
+    c = GOLD_INST[name]
+    kind, B, C, H, W, R, heads, box, seed = c["case"]
+    m = SM.make_model(kind, C, R, heads, box, seed)
+    m.load_state_dict(c["state"])
+    x = c["x"]
+    with torch.no_grad():
+        phi = m.pre_activation(x)
+        table = m._collect_shifts()
+        w = torch.stack(m._weights(phi, table), 0)
+        mat = m._head_mix_matrix()
+        w = torch.stack([m._mix_heads(w[i], C, mat) for i in range(len(table))], 0)
+    if kind == "gasd":
+        if box:
+            w = w * torch.stack([O.box_mask(H, W, dx, dy, w.dtype)
+                                 for dx, dy in table])[:, None, None]
+        sh = torch.tensor([(dx, dy, 0) for dx, dy in table])
+        D, L = O.normalized_accumulate_uz(x, w.reshape(-1, C, H, W), sh, False)
+        _close(D, c["D"], 1e-12, 1e-12)
+        _close(L.exp(), c["Z"], 1e-12, 1e-12)
+    elif kind == "nekde":
+        rows = [(dx, dy, (1 if box else 2) if inv else 0) for dx, dy, inv in table]
+        if box:
+            w = w * torch.stack([O.box_mask(H, W, dx, dy, w.dtype)
+                                 for dx, dy, _ in table])[:, None, None]
+        U, Z = O.accumulate_uz(x, w.reshape(-1, C, H, W), rows)
+        _close(U / Z, c["D"], 1e-12, 1e-12)
+        _close(Z, c["Z"], 1e-12, 1e-12)
+    else:
+        Wx, dh = O.metropolis_aggregate(w.permute(1, 0, 2, 3, 4), x, table, box,
+                                        1e-6)
+        _close(Wx, c["Wx"], 1e-12, 1e-12)
+        _close(dh, c["d_hat"], 1e-12, 1e-12)
