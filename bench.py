@@ -539,8 +539,116 @@ def _wl_metropolis():
         "f32", make, cpu)
 
 
+def _nectr_model(dev, dtype):
+    """NECTR model 1 with the benchmark configuration (concat, residual
+    depth 2, projection depth 1, latent 16, patch radius 1, window radius 5,
+    one channel, blind, exp head), random init (seed 0), NECTR installer
+    applied."""
+    from types import SimpleNamespace
+    from neural_shift_cuda_b200.integration import install_cuda_shift_nectr
+    from neural_shift_cuda_b200.integration.nectr_models1 import NECTR_denoiser
+    args = SimpleNamespace(model_type="concat", residual_depth=2, proj_depth=1,
+                           latent_dim=16, patch_rad=1, output_activation="exp",
+                           window_rad=5, in_channel=1, blind=True)
+    cls = type("NECTRBench", (NECTR_denoiser,), {})
+    install_cuda_shift_nectr(cls)
+    torch.manual_seed(0)
+    m = cls(args)
+    return m.to(device=dev, dtype=dtype).eval()
+
+
+def _wl_nectr(dtype_name):
+    Bt, Hs, Ws, Rr = 8, 256, 256, 5
+    rows = halfplane(Rr)
+    Sn = len(rows)
+    dtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+
+    def noisy(g, sh, dev):
+        return (torch.rand(sh, generator=g, device=dev)
+                + (25 / 255) * torch.randn(sh, generator=g, device=dev))
+
+    def make(dev, b0, nb):
+        from neural_shift_cuda_b200.integration import nectr_patch as NP
+        m = _nectr_model(dev, dtype)
+        x = _seeded((1, Hs, Ws), b0, nb, 7, dev,
+                    lambda g, sh: noisy(g, sh, dev)).to(dtype)
+
+        def run(xi):
+            with torch.no_grad():
+                return m(xi)
+
+        def per_kernel(xi):
+            """One forward with CUDA events around the two kernels of the
+            path (pair_gather, normalized_accumulate_uz): median of 5."""
+            names = {"pair_gather": [], "normalized_accumulate_uz": []}
+            sizes = {}
+            orig = {k: getattr(NP, k) for k in names}
+
+            def wrap(k):
+                def f(*a, **kw):
+                    st = torch.cuda.current_stream()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    out = orig[k](*a, **kw)
+                    e1.record(st)
+                    names[k].append((e0, e1))
+                    sizes[k] = _nbytes([t for t in a if isinstance(t, torch.Tensor)]
+                                       ) + _nbytes(out)
+                    return out
+                return f
+            try:
+                for k in names:
+                    setattr(NP, k, wrap(k))
+                for _ in range(5):
+                    run(xi)
+            finally:
+                for k in names:
+                    setattr(NP, k, orig[k])
+            torch.cuda.synchronize()
+            res = {}
+            for k, evs in names.items():
+                ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+                res[k] = {"ms": ms, "algorithmic_bytes": sizes[k]}
+            # pair_gather's guide input is (B, L, H, W) and its outputs the
+            # (S*B, 2L, H, W) pair batch and (S*B, 1, H, W) mask: the sum above
+            # counts the guide, pair batch and mask once each; the normalized
+            # reduction counts x, the (S*B, 1, H, W) values, D and log_C.
+            return res
+
+        return dict(inputs=[x], run=run, launches=2,
+                    units=Sn * nb * 1 * Hs * Ws, per_kernel=per_kernel,
+                    dominant="pair_gather")
+
+    def cpu(nb):
+        dev = torch.device("cpu")
+        m = _nectr_model(dev, torch.float32)
+        g = torch.Generator().manual_seed(0)
+        x = noisy(g, (1, 1, Hs, Ws), dev)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            m(x)     # CPU input: the model's own serial forward
+        return (Sn * 1 * Hs * Ws, time.perf_counter() - t0,
+                f"NECTR_models1 serial forward (the reference model's own "
+                f"per-shift loop) on 1 of {Bt} images, fp32, torch CPU")
+
+    return OpWorkload(
+        "nectr_" + dtype_name,
+        f"pixel-shifts/s (NECTR model-1 patched forward, configs[1]: x "
+        f"(8,1,256,256) {dtype_name}, latent 16, R=5 S=61)", Bt,
+        {"workload": f"NECTR_models1 patched forward (pair_gather -> weight "
+                     f"head -> normalized_accumulate_uz, log mode), x "
+                     f"(8,1,256,256) {dtype_name} U[0,1]+N(0,(25/255)^2), "
+                     f"concat, residual_depth 2, proj_depth 1, latent 16, "
+                     f"R=5 S=61, random init (configs[1])",
+         "unit_definition": "S*B*C*H*W of the aggregation per forward"},
+        f"{dtype_name} model, f32 accumulate", make, cpu)
+
+
 WORKLOADS = {"pair_gather": _wl_pair_gather, "normalized": _wl_normalized,
-             "metropolis": _wl_metropolis}
+             "metropolis": _wl_metropolis,
+             "nectr": lambda: _wl_nectr("f32"),
+             "nectr_bf16": lambda: _wl_nectr("bf16")}
 
 
 def _nbytes(ts):
@@ -632,6 +740,16 @@ def run_workload(args, wl):
     step_ms = [a.elapsed_time(b) for a, b in ev]
     kern_ms = statistics.median(step_ms)
     alg = _nbytes(inputs) + _nbytes(out)
+    kernels = None
+    roof_note = "step time of all launches of the op (per rank)"
+    if "per_kernel" in w:
+        kernels = w["per_kernel"](*inputs)
+        dom = kernels[w["dominant"]]
+        kern_ms, alg = dom["ms"], dom["algorithmic_bytes"]
+        roof_note = (f"dominant kernel {w['dominant']}, CUDA events around its "
+                     f"call inside the forward (per rank)")
+        for k in kernels.values():
+            k["achieved_gbs"] = k["algorithmic_bytes"] / (k["ms"] * 1e-3) / 1e9
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -639,6 +757,9 @@ def run_workload(args, wl):
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = alg / (kern_ms * 1e-3) / 1e9
+    if kernels:
+        for k in kernels.values():
+            k["frac"] = k["achieved_gbs"] / peak
 
     e2e = None
     if not args.no_e2e:
@@ -704,7 +825,8 @@ def run_workload(args, wl):
                          "kernel_ms": kern_ms, "algorithmic_bytes": alg,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
                          if peaks else "fallback 6650 GB/s",
-                         "note": "step time of all launches of the op (per rank)"},
+                         "note": roof_note},
+            "kernels": kernels,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": w["launches"] * args.steps,
             "step_ms": {"min": min(step_ms), "median": kern_ms, "max": max(step_ms)},

@@ -13,7 +13,10 @@
  *     has_inv 0 = no mirror term, 1 = masked mirror (the reference's
  *     meaning), 2 = periodic mirror (extension, accumulate / normalized:
  *     the mirror term reads (p - d) mod (H, W) with no inside test; not
- *     accepted by the row-band entry points);
+ *     accepted by the row-band entry points), 3 = transposed row
+ *     (extension, accumulate_uz only: the row adds w_s(p - d) x(p - d)
+ *     read circularly and no forward term -- K^T of the forward-only row
+ *     without a rolled copy of the weight plane);
  *   - inputs keep their storage dtype (fp16/bf16/fp32 are read natively and
  *     promoted in registers; fp64 stays fp64) instead of being copied to a
  *     promoted tensor first;

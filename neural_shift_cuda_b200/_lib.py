@@ -172,10 +172,25 @@ class HostShifts:
         return [tuple(int(v) for v in r) for r in self.t.tolist()]
 
 
-def mirror_mode(hs: HostShifts, periodic: bool) -> HostShifts:
+def mirror_mode(hs: HostShifts, periodic: bool, transpose: bool = False) -> HostShifts:
     """The table as the library reads it: column 2 becomes 0 (no mirror),
     1 (masked mirror, the reference's meaning of any nonzero value) or, with
-    periodic=True, 2 (periodic mirror) for every row with a mirror term."""
+    periodic=True, 2 (periodic mirror) for every row with a mirror term.
+    transpose=True turns every (forward-only) row into 3: the row then adds
+    w_s(p - d) x(p - d), read circularly, and no forward term."""
+    if transpose:
+        if hs.cols == 3 and bool((hs.t[:, 2] != 0).any()):
+            raise ValueError("transpose=True needs forward-only rows "
+                             "(has_inv == 0 on every row)")
+        key = "T"
+        hit = hs.modes.get(key)
+        if hit is None:
+            t = torch.zeros((hs.S, 3), dtype=torch.int64)
+            t[:, :2] = hs.t[:, :2]
+            t[:, 2] = 3
+            hit = HostShifts(t.contiguous())
+            hs.modes[key] = hit
+        return hit
     if hs.cols != 3:
         return hs
     key = bool(periodic)

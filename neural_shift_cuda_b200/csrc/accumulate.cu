@@ -68,12 +68,14 @@ acc_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
         for (int s = 0; s < st.S; ++s) {
             const int64_t dx = st.dx[s], dy = st.dy[s];
             const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane_o;
-            const A wv = ldg_acc<TW, A>(ws + h * W + wcol);
-            const int64_t xo = xr.fwd(h + dx) * W + wrap1(wcol + dy, W);
+            if (st.has_fwd(s)) {
+                const A wv = ldg_acc<TW, A>(ws + h * W + wcol);
+                const int64_t xo = xr.fwd(h + dx) * W + wrap1(wcol + dy, W);
 #pragma unroll
-            for (int i = 0; i < NC; ++i)
-                if (i < nc) u[i] += wv * ldg_acc<TX, A>(xb + i * plane_x + xo);
-            z += wv;
+                for (int i = 0; i < NC; ++i)
+                    if (i < nc) u[i] += wv * ldg_acc<TX, A>(xb + i * plane_x + xo);
+                z += wv;
+            }
             if (st.has_inv(s)) {
                 const bool per = st.has_per(s);   // full-image calls only
                 const int64_t hm = per ? wrap1(h - dx, Hout) : h - dx;
@@ -249,18 +251,21 @@ acc_bwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
             const int64_t dx = st.dx[s], dy = st.dy[s];
             const int64_t wbase = ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
             const TW* ws = w + wbase;
-            // forward term of output q - d (circular) reads x(q)
-            const int64_t qs = wrap1(h - dx, H) * W + wrap1(wcol - dy, W);
-            const A w_src = ldg_acc<TW, A>(ws + qs);
-            // grad_w forward part: x(q+d) gU(q) + gZ(q)
-            const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
-            A gws = gz_q;
+            A gws = A(0);
+            if (st.has_fwd(s)) {
+                // forward term of output q - d (circular) reads x(q)
+                const int64_t qs = wrap1(h - dx, H) * W + wrap1(wcol - dy, W);
+                const A w_src = ldg_acc<TW, A>(ws + qs);
+                // grad_w forward part: x(q+d) gU(q) + gZ(q)
+                const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
+                gws = gz_q;
 #pragma unroll
-            for (int i = 0; i < NC; ++i)
-                if (i < nc) {
-                    acc[i] += w_src * gU[cb + i * plane + qs];
-                    gws += ldg_acc<TX, A>(x + cb + i * plane + qf) * gu_q[i];
-                }
+                for (int i = 0; i < NC; ++i)
+                    if (i < nc) {
+                        acc[i] += w_src * gU[cb + i * plane + qs];
+                        gws += ldg_acc<TX, A>(x + cb + i * plane + qf) * gu_q[i];
+                    }
+            }
             if (st.has_inv(s) && (st.has_per(s) || (inb(h + dx, H) && inb(wcol + dy, W)))) {
                 const A w_q = ldg_acc<TW, A>(ws + q);
                 const int64_t qi = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
@@ -303,10 +308,11 @@ acc_bwd_gw_bcast_kernel(const TX* __restrict__ x,
             const int64_t qf = wrap1(h + dx, H) * W + wrap1(wcol + dy, W);
             const bool mir = st.has_inv(s) &&
                              (st.has_per(s) || (inb(h + dx, H) && inb(wcol + dy, W)));
+            const bool fwd = st.has_fwd(s);
             A gws = A(0);
             for (int64_t c = 0; c < C; ++c) {
                 const int64_t co = cb + c * plane;
-                gws += ldg_acc<TX, A>(x + co + qf) * gU[co + q] + gZ[co + q];
+                if (fwd) gws += ldg_acc<TX, A>(x + co + qf) * gU[co + q] + gZ[co + q];
                 if (mir)
                     gws += ldg_acc<TX, A>(x + co + q) * gU[co + qf] + gZ[co + qf];
             }

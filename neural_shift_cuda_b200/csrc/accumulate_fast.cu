@@ -19,10 +19,10 @@
 namespace nsc {
 namespace fast {
 
-template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT, int MODE>
 bool launch(const WMaps& maps, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
-            cudaStream_t stream);
+            int* invalid, cudaStream_t stream);
 
 }  // namespace fast
 
@@ -45,11 +45,12 @@ int sm_count() {
     return cache[dev];
 }
 
-template <typename T, int NC>
-bool by_bucket(bool exact, int K, const fast::WMaps& maps,
-               const void* x, void* U, void* Z, const fast::FastTable& tab,
-               const fast::Geo& g, unsigned int* to, cudaStream_t st) {
-#define NSC_B(A, B, E) return fast::launch<T, NC, A, B, E>(maps, x, U, Z, tab, g, to, st)
+template <typename T, int NC, int M>
+bool by_bucket_m(bool exact, int K, const fast::WMaps& maps,
+                 const void* x, void* U, void* Z, const fast::FastTable& tab,
+                 const fast::Geo& g, unsigned int* to, int* inv, cudaStream_t st) {
+#define NSC_B(A, B, E) \
+    return fast::launch<T, NC, A, B, E, M>(maps, x, U, Z, tab, g, to, inv, st)
     if (exact) {
         switch (K) {
             case 2: NSC_B(0, 2, true);
@@ -69,14 +70,24 @@ bool by_bucket(bool exact, int K, const fast::WMaps& maps,
 #undef NSC_B
 }
 
+template <typename T, int NC>
+bool by_bucket(int mode, bool exact, int K, const fast::WMaps& maps,
+               const void* x, void* U, void* Z, const fast::FastTable& tab,
+               const fast::Geo& g, unsigned int* to, int* inv, cudaStream_t st) {
+    if (mode == 1) return by_bucket_m<T, NC, 1>(exact, K, maps, x, U, Z, tab, g, to, inv, st);
+    if (mode == 2) return by_bucket_m<T, NC, 2>(exact, K, maps, x, U, Z, tab, g, to, inv, st);
+    return by_bucket_m<T, NC, 0>(exact, K, maps, x, U, Z, tab, g, to, inv, st);
+}
+
 }  // namespace
 
 bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                   int64_t B, int64_t C, int64_t Hout, int64_t W, int64_t x_rows,
                   int64_t x_off, int wrap, const ShiftTable& st, void* U, void* Z,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, int mode, int* invalid) {
     using namespace fast;
     g_decline = "";
+    if (mode != 0 && !wrap) DECLINE("normalized modes take full images only");
     if (std::getenv("NSC_DISABLE_FAST")) DECLINE("disabled by NSC_DISABLE_FAST");
     if (st.any_per) DECLINE("periodic mirror rows");
     if (xd != wd || (xd != NSC_F16 && xd != NSC_BF16 && xd != NSC_F32)) DECLINE("dtype");
@@ -232,14 +243,15 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     unsigned int* to = wait_timeout_counter();
     if (!to) DECLINE("timeout counter");
     (void)sm_count;
+    const int m = mode;
     if (xd == NSC_F16)
-        return NC == 1 ? by_bucket<__half, 1>(exact, K, maps, x, U, Z, tab, g, to, stream)
-                       : by_bucket<__half, 3>(exact, K, maps, x, U, Z, tab, g, to, stream);
+        return NC == 1 ? by_bucket<__half, 1>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream)
+                       : by_bucket<__half, 3>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream);
     if (xd == NSC_BF16)
-        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(exact, K, maps, x, U, Z, tab, g, to, stream)
-                       : by_bucket<__nv_bfloat16, 3>(exact, K, maps, x, U, Z, tab, g, to, stream);
-    return NC == 1 ? by_bucket<float, 1>(exact, K, maps, x, U, Z, tab, g, to, stream)
-                   : by_bucket<float, 3>(exact, K, maps, x, U, Z, tab, g, to, stream);
+        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream)
+                       : by_bucket<__nv_bfloat16, 3>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream);
+    return NC == 1 ? by_bucket<float, 1>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream)
+                   : by_bucket<float, 3>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream);
 }
 
 int fast_sm_count() { return sm_count(); }

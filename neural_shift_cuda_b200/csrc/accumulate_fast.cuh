@@ -35,6 +35,23 @@
 // Summation order: per output, shifts in (dx, dy) order, forward before
 // mirror, fp32 accumulation -- within the fp32 tolerance of the
 // reference's pairwise tree (ops.py:77-92).
+//
+// MODE selects what is accumulated per output pixel (same tiles, copies and
+// windows):
+//   0  accumulate_uz: U = sum w x, Z = sum w;
+//   1  normalized_accumulate_uz, log weights (logits k): D = sum a x / sum a,
+//      log_C = log sum e^k, a = 2^(k log2(e) - m) with a lazy running
+//      reference m (moved only when a key would give a > 2^16, the partial
+//      sums rescaled by 2^(m_old - m_new)), the online normalisation of
+//      Milakov & Gimelshein (2018);
+//   2  normalized_accumulate_uz, positive weights: a = k 2^-e with a lazy
+//      power-of-two scale, rescaled the same way (exact scaling).
+// In modes 1 and 2 a mirror key outside the image contributes nothing: the
+// TMA zero fill is already "no weight" for positive keys; log keys are
+// masked to -inf on border tiles from the same inside test that zeroes the
+// mirror x window.  A NaN / +inf key (negative positive-mode key) poisons
+// the pixel: D and log_C NaN and the invalid flag set; a pixel without a
+// live key gives D = 0, log_C = -inf (reference shift_ops_cuda.cu:528-653).
 #pragma once
 
 // Up to this many consecutive weight planes (same dx, consecutive plane
@@ -205,6 +222,108 @@ __device__ __forceinline__ void add_e(float& acc, const uint32_t* w) {
     }
 }
 
+// Compile-time loop helper: f(std::integral_constant<int, I>) for I in [0, N).
+template <int I, int N, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (I < N) {
+        f(std::integral_constant<int, I>{});
+        static_for<I + 1, N>(f);
+    }
+}
+
+// Element I of packed words as fp32.
+template <typename T, int I>
+__device__ __forceinline__ float elem_f(const uint32_t* w) {
+    if constexpr (Elem<T>::kind == 2) {
+        return __uint_as_float(w[I]);
+    } else if constexpr (Elem<T>::kind == 1) {
+        const uint32_t v = w[I >> 1];
+        return __uint_as_float((I & 1) ? (v & 0xFFFF0000u) : (v << 16));
+    } else {
+        const uint32_t v = w[I >> 1];
+        return __half2float(__ushort_as_half(
+            static_cast<unsigned short>((I & 1) ? (v >> 16) : (v & 0xFFFFu))));
+    }
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kLazy = 16.0f;        // log mode: rescale when a > 2^16
+constexpr float kPosLazy = 65536.0f;  // positive mode: the same bound
+
+__device__ __forceinline__ float ex2_fast(float v) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
+// Modes 1 / 2: add V keys (key element KI + i of `kw`, image element XI + i
+// of `xw[c]`) to the per-pixel online sums.  MASK: image element XI + i is
+// a mirror source; bit (XI + i) of `valid` says it is inside the image.
+template <typename T, int MODE, int NC, int V, int KI, int XI, bool MASK, int NX>
+__device__ __forceinline__ void norm_keys(const uint32_t* kw, const uint32_t (&xw)[NC][NX],
+                                          float (&u)[NC][V], float (&z)[V],
+                                          float (&mr)[V], uint64_t valid) {
+    float a[V];
+    float amax = -INFINITY, amin = INFINITY;
+    static_for<0, V>([&](auto ic) {
+        constexpr int i = decltype(ic)::value;
+        const float key = elem_f<T, KI + i>(kw);
+        if constexpr (MODE == 1) {
+            a[i] = fmaf(key, kLog2e, -mr[i]);
+            if constexpr (MASK)
+                a[i] = ((valid >> (XI + i)) & 1ull) ? a[i] : -INFINITY;
+        } else {
+            a[i] = key * mr[i];
+            amin = fminf(amin, a[i]);
+        }
+        asm("max.NaN.f32 %0, %0, %1;" : "+f"(amax) : "f"(a[i]));
+    });
+    const bool need = MODE == 1 ? !(amax <= kLazy) : (!(amax <= kPosLazy) || amin < 0.f);
+    if (__builtin_expect(__any_sync(0xffffffffu, need), 0)) {
+        static_for<0, V>([&](auto ic) {
+            constexpr int i = decltype(ic)::value;
+            const float key = elem_f<T, KI + i>(kw);
+            if constexpr (MODE == 1) {
+                if (a[i] > kLazy) {          // false for NaN keys: they poison below
+                    const float mn = key * kLog2e;
+                    const float f = ex2_fast(mr[i] - mn);
+                    z[i] *= f;
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) u[c][i] *= f;
+                    mr[i] = mn;
+                    a[i] = fmaf(key, kLog2e, -mn);
+                }
+            } else {
+                if (!(a[i] <= kPosLazy) || a[i] < 0.f) {
+                    if (!(key >= 0.f) || key == INFINITY) {
+                        z[i] = __int_as_float(0x7fffffff);   // poison: NaN
+                        a[i] = 0.f;
+                    } else {
+                        // binary exponent of the key (subnormals clamp below)
+                        int e = static_cast<int>((__float_as_uint(key) >> 23) & 0xFFu) - 127;
+                        e = e < -100 ? -100 : (e > 126 ? 126 : e);
+                        const float sc = __int_as_float((127 - e) << 23);
+                        const float keep = mr[i] == INFINITY ? 0.f : sc / mr[i];
+                        z[i] *= keep;
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) u[c][i] *= keep;
+                        mr[i] = sc;
+                        a[i] = key * sc;
+                    }
+                }
+            }
+        });
+    }
+    static_for<0, V>([&](auto ic) {
+        constexpr int i = decltype(ic)::value;
+        const float ai = MODE == 1 ? ex2_fast(a[i]) : a[i];
+        z[i] += ai;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) u[c][i] = fmaf(ai, elem_f<T, XI + i>(xw[c]), u[c][i]);
+    });
+}
+
 template <int N>
 __device__ __forceinline__ void lds_words(uint32_t (&dst)[N], const void* src, int word0 = 0) {
     static_assert(N % 4 == 0, "16-byte granules");
@@ -223,14 +342,6 @@ __device__ __forceinline__ int64_t pmod(int64_t a, int64_t n) {
     return r < 0 ? r + n : r;
 }
 
-// Compile-time loop helper: f(std::integral_constant<int, I>) for I in [0, N).
-template <int I, int N, typename F>
-__device__ __forceinline__ void static_for(F&& f) {
-    if constexpr (I < N) {
-        f(std::integral_constant<int, I>{});
-        static_for<I + 1, N>(f);
-    }
-}
 
 // 16 / 8 / 4-byte shared-memory loads by 32-bit shared address.  volatile
 // keeps them ordered after the mbarrier waits (also volatile asm).
@@ -320,12 +431,13 @@ __device__ __forceinline__ void load_win(uint32_t (&d)[N], const uint32_t* p) {
 // with a mirror term for dx != 0; weight planes consecutive along dy), so
 // which entries exist, which have a mirror term and how they group into
 // copies are compile-time facts of dy and need no per-shift table tests.
-template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT, int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
 acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 float* __restrict__ U, float* __restrict__ Zo, const FastTable tab,
                 const Geo g, unsigned int* timeouts,
-                unsigned long long* __restrict__ ticket) {
+                unsigned long long* __restrict__ ticket, int* __restrict__ invalid) {
+    // modes 1 / 2: U receives D and Zo receives log_C
     constexpr int V = 16 / static_cast<int>(sizeof(T));
     constexpr int EPW = 4 / static_cast<int>(sizeof(T));   // elements per word
     constexpr int TW = TPR * V;
@@ -528,10 +640,12 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         }
         const int64_t next = tile_at(k + 1);
 
-        float u[NC][V], z[V];
+        float u[NC][V], z[V], mr[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) {
             z[i] = 0.f;
+            // modes 1 / 2: running reference (log2 units) / scale 2^-e (inf: unset)
+            mr[i] = MODE == 1 ? -3.0e38f : INFINITY;
 #pragma unroll
             for (int c = 0; c < NC; ++c) u[c][i] = 0.f;
         }
@@ -540,6 +654,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         for (int dx = -Rx; dx <= Rx; ++dx) {
             if (!tab.row_any[dx + MAXR]) continue;
             uint32_t xf[NC][FWH - FWL], xm[NC][MWH - MWL];
+            uint64_t mvalid = ~0ull;   // mirror window elements inside the image
             const uint32_t xa32 = smem_u32(xa) + static_cast<uint32_t>(tc * V * sizeof(T));
             const uint32_t xrow = static_cast<uint32_t>(XH * XW * sizeof(T));
 #pragma unroll
@@ -559,6 +674,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                     for (int k = 0; k < (MWH - MWL) * EPW; ++k) {
                         const int64_t gc = gcol0 + MWL * EPW + k;
                         if (!rin || gc < 0 || gc >= g.W) {
+                            mvalid &= ~(1ull << k);
                             const uint32_t keep =
                                 EPW == 1 ? 0u : ((k & 1) ? 0x0000FFFFu : 0xFFFF0000u);
 #pragma unroll
@@ -587,13 +703,18 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];
                 lds_words32<V / EPW>(wv, sp + off_main + mo * sizeof(T));
-                static_for<0, V>([&](auto ic) {
-                    constexpr int i = decltype(ic)::value;
+                if constexpr (MODE == 0) {
+                    static_for<0, V>([&](auto ic) {
+                        constexpr int i = decltype(ic)::value;
 #pragma unroll
-                    for (int c = 0; c < NC; ++c)
-                        fma_e<T, i, XC + dy + i - FWL * EPW>(u[c][i], wv, xf[c]);
-                    add_e<T, i>(z[i], wv);
-                });
+                        for (int c = 0; c < NC; ++c)
+                            fma_e<T, i, XC + dy + i - FWL * EPW>(u[c][i], wv, xf[c]);
+                        add_e<T, i>(z[i], wv);
+                    });
+                } else {
+                    norm_keys<T, MODE, NC, V, 0, XC + dy - FWL * EPW, false>(
+                        wv, xf, u, z, mr, 0ull);
+                }
                 if (inv) {
                     constexpr int moff = mo - dy;               // >= 0
                     constexpr int kk = moff % V;
@@ -602,13 +723,18 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                     lds_words32<V / EPW>(mw, sp + off_mir + mb * sizeof(T));
                     if constexpr (kk != 0)
                         lds_words32<V / EPW>(mw + V / EPW, sp + off_mir + (mb + V) * sizeof(T));
-                    static_for<0, V>([&](auto ic) {
-                        constexpr int i = decltype(ic)::value;
+                    if constexpr (MODE == 0) {
+                        static_for<0, V>([&](auto ic) {
+                            constexpr int i = decltype(ic)::value;
 #pragma unroll
-                        for (int c = 0; c < NC; ++c)
-                            fma_e<T, kk + i, XC - dy + i - MWL * EPW>(u[c][i], mw, xm[c]);
-                        add_e<T, kk + i>(z[i], mw);
-                    });
+                            for (int c = 0; c < NC; ++c)
+                                fma_e<T, kk + i, XC - dy + i - MWL * EPW>(u[c][i], mw, xm[c]);
+                            add_e<T, kk + i>(z[i], mw);
+                        });
+                    } else {
+                        norm_keys<T, MODE, NC, V, kk, XC - dy - MWL * EPW, MODE == 1>(
+                            mw, xm, u, z, mr, mvalid);
+                    }
                 }
                 if (last) {   // copy fully used: release it
                     __syncwarp();
@@ -649,6 +775,33 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         // ---- store
         const int64_t h = h0 + tr;
         const int64_t wcol = w0 + tc * V;
+        if constexpr (MODE != 0) {
+            // D = sum a x / sum a, log_C = reference + log(sum a); special
+            // values as in the general kernel
+            bool bad = false;
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                const float sv = z[i];
+                if (sv != sv) {
+                    bad = true;
+                    z[i] = __int_as_float(0x7fffffff);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) u[c][i] = z[i];
+                } else if (sv == 0.f) {
+                    z[i] = -INFINITY;
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) u[c][i] = 0.f;
+                } else {
+                    const float base = MODE == 1
+                        ? mr[i] * kLn2
+                        : -static_cast<float>(static_cast<int>((__float_as_uint(mr[i]) >> 23) & 0xFFu) - 127) * kLn2;
+                    z[i] = base + logf(sv);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) u[c][i] = u[c][i] / sv;
+                }
+            }
+            if (bad && invalid && h < g.H && wcol < g.W) atomicOr(invalid, 1);
+        }
         if (h < g.H && wcol < g.W) {
 #pragma unroll
             for (int c = 0; c < NC; ++c) {

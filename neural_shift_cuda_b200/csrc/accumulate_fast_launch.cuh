@@ -14,10 +14,10 @@ void fast_set_decline(const char* why);
 
 namespace fast {
 
-template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT, int MODE>
 bool launch(const WMaps& maps, const void* x, void* U, void* Z,
             const FastTable& tab, Geo g, unsigned int* timeouts,
-            cudaStream_t stream) {
+            int* invalid, cudaStream_t stream) {
     unsigned long long* ticket = tile_ticket(stream);
     if (!ticket) {
         fast_set_decline("tile counter");
@@ -37,7 +37,7 @@ bool launch(const WMaps& maps, const void* x, void* U, void* Z,
     if (ns > 12) ns = 12;
     g.nstage = static_cast<int32_t>(ns);
     const size_t smem = fixed + ns * per_stage;
-    auto k = acc_fast_kernel<T, NC, DYMIN, DYMAX, EXACT>;
+    auto k = acc_fast_kernel<T, NC, DYMIN, DYMAX, EXACT, MODE>;
     cudaFuncAttributes attr;
     if (cudaFuncGetAttributes(&attr, k) != cudaSuccess ||
         attr.maxThreadsPerBlock < NTHREADS) {
@@ -59,20 +59,24 @@ bool launch(const WMaps& maps, const void* x, void* U, void* Z,
     const unsigned grid = static_cast<unsigned>(g.ntiles < nsm ? g.ntiles : nsm);
     k<<<grid, NTHREADS, smem, stream>>>(maps, static_cast<const T*>(x),
                                         static_cast<float*>(U),
-                                        static_cast<float*>(Z), tab, g, timeouts, ticket);
+                                        static_cast<float*>(Z), tab, g, timeouts, ticket,
+                                        invalid);
     return true;
 }
 
 }  // namespace fast
 }  // namespace nsc
 
-#define NSC_FAST_ONE(T, NC, A, B, E)                                               \
-    template bool nsc::fast::launch<T, NC, A, B, E>(const WMaps&,                    \
+#define NSC_FAST_ONE(T, NC, A, B, E, M)                                            \
+    template bool nsc::fast::launch<T, NC, A, B, E, M>(const WMaps&,                 \
         const void*, void*, void*, const FastTable&, Geo,                            \
-        unsigned int*, cudaStream_t);
-#define NSC_FAST_INSTANTIATE(T, NC)                                                  \
-    NSC_FAST_ONE(T, NC, 0, 2, true) NSC_FAST_ONE(T, NC, 0, 4, true)                  \
-    NSC_FAST_ONE(T, NC, 0, 6, true) NSC_FAST_ONE(T, NC, 0, 8, true)                  \
-    NSC_FAST_ONE(T, NC, 0, 10, true) NSC_FAST_ONE(T, NC, 0, 12, true)                \
-    NSC_FAST_ONE(T, NC, 0, 16, true) NSC_FAST_ONE(T, NC, -4, 4, false)               \
-    NSC_FAST_ONE(T, NC, -8, 8, false) NSC_FAST_ONE(T, NC, -12, 12, false)
+        unsigned int*, int*, cudaStream_t);
+// Every table bucket of one storage type, image-channel count and mode
+// (0: accumulate_uz, 1: normalized log weights, 2: normalized positive).
+#define NSC_FAST_INSTANTIATE_MODE(T, NC, M)                                          \
+    NSC_FAST_ONE(T, NC, 0, 2, true, M) NSC_FAST_ONE(T, NC, 0, 4, true, M)            \
+    NSC_FAST_ONE(T, NC, 0, 6, true, M) NSC_FAST_ONE(T, NC, 0, 8, true, M)            \
+    NSC_FAST_ONE(T, NC, 0, 10, true, M) NSC_FAST_ONE(T, NC, 0, 12, true, M)          \
+    NSC_FAST_ONE(T, NC, 0, 16, true, M) NSC_FAST_ONE(T, NC, -4, 4, false, M)         \
+    NSC_FAST_ONE(T, NC, -8, 8, false, M) NSC_FAST_ONE(T, NC, -12, 12, false, M)
+#define NSC_FAST_INSTANTIATE(T, NC) NSC_FAST_INSTANTIATE_MODE(T, NC, 0)

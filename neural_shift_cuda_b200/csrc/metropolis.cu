@@ -338,7 +338,13 @@ nsc_status check_metro(const char* op, int64_t Cw, int64_t B, int64_t C,
                     op, (long long)Cw, (long long)C);
     if (!(eps > 0.0) || !std::isfinite(eps))
         return fail(NSC_ERR_INVALID_ARG, "%s: eps must be finite and > 0", op);
-    return build_shifts(op, shifts, S, 3, H, W, st);
+    nsc_status e2 = build_shifts(op, shifts, S, 3, H, W, st);
+    if (e2) return e2;
+    if (st->any_tr)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: transposed rows (column value 3) are accepted by "
+                    "accumulate_uz only", op);
+    return ok();
 }
 
 // Geometry of the tiled kernels, or false when the call stays on the

@@ -22,6 +22,7 @@
 #include "nsc_common.cuh"
 #include "normalized_fast.h"
 #include "nsc_host.h"
+#include "accumulate.h"
 
 namespace nsc {
 namespace {
@@ -332,7 +333,13 @@ nsc_status check_common(const char* op, int xd, int wd, int64_t Cw, int64_t B,
                     "%s: weights must be (S*B, C, H, W) or channel-broadcast "
                     "(S*B, 1, H, W); got w_channels=%lld with C=%lld",
                     op, (long long)Cw, (long long)C);
-    return build_shifts(op, shifts, S, 3, H, W, st);
+    nsc_status e2 = build_shifts(op, shifts, S, 3, H, W, st);
+    if (e2) return e2;
+    if (st->any_tr)
+        return fail(NSC_ERR_INVALID_ARG,
+                    "%s: transposed rows (column value 3) are accepted by "
+                    "accumulate_uz only", op);
+    return ok();
 }
 
 }  // namespace
@@ -358,9 +365,14 @@ nsc_status nsc_normalized_accumulate_uz_fwd(
     if (norm_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, st,
                       log_weights ? 1 : 0, D, log_C, invalid_flag, sm))
         return check_launch(op);
+    // tables with mirror terms: the TMA-tiled kernel in its normalized modes
+    if (!getenv("NSC_NORM_GENERIC") &&
+        acc_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0, 1, st,
+                     D, log_C, sm, log_weights ? 1 : 2, invalid_flag))
+        return check_launch(op);
     if (getenv("NSC_REQUIRE_FAST"))
-        return fail(NSC_ERR_INVALID_ARG, "%s: tiled path declined: %s", op,
-                    norm_fast_decline_reason());
+        return fail(NSC_ERR_INVALID_ARG, "%s: tiled paths declined: %s; %s", op,
+                    norm_fast_decline_reason(), fast_decline_reason());
     return with_types(op, x_dtype, w_dtype, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;

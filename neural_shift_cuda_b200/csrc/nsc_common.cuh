@@ -33,7 +33,9 @@ struct ShiftTable {
     int32_t dy[kMaxShifts];
     uint32_t inv[kMaxShifts / 32];
     uint32_t per[kMaxShifts / 32];   // mirror term periodic (column value 2)
+    uint32_t nofwd[kMaxShifts / 32]; // no forward term (column value 3)
     int32_t any_per;
+    int32_t any_tr;                  // some row has column value 3
     __host__ __device__ __forceinline__ bool has_inv(int s) const {
         return (inv[s >> 5] >> (s & 31)) & 1u;
     }
@@ -42,6 +44,13 @@ struct ShiftTable {
     // reference's row encoding: column value 2).
     __host__ __device__ __forceinline__ bool has_per(int s) const {
         return (per[s >> 5] >> (s & 31)) & 1u;
+    }
+    // Transposed row (column value 3, accumulate_uz only): the row
+    // contributes w_s(p - d) x(p - d) read circularly and no forward term --
+    // the transpose of the forward-only row (dx, dy, 0) with the same
+    // weight plane.
+    __host__ __device__ __forceinline__ bool has_fwd(int s) const {
+        return !((nofwd[s >> 5] >> (s & 31)) & 1u);
     }
 };
 

@@ -59,8 +59,9 @@ inline nsc_status build_shifts(const char* op, const int64_t* shifts,
     if (!shifts) return fail(NSC_ERR_INVALID_ARG, "%s: shifts is NULL", op);
     st->S = static_cast<int32_t>(S);
     st->R = 0;
-    for (int i = 0; i < kMaxShifts / 32; ++i) st->inv[i] = st->per[i] = 0;
+    for (int i = 0; i < kMaxShifts / 32; ++i) st->inv[i] = st->per[i] = st->nofwd[i] = 0;
     st->any_per = 0;
+    st->any_tr = 0;
     for (int64_t s = 0; s < S; ++s) {
         const int64_t dx = shifts[s * cols + 0];
         const int64_t dy = shifts[s * cols + 1];
@@ -73,10 +74,18 @@ inline nsc_status build_shifts(const char* op, const int64_t* shifts,
                         (long long)H, (long long)W);
         st->dx[s] = static_cast<int32_t>(dx);
         st->dy[s] = static_cast<int32_t>(dy);
+        if (iv < 0 || iv > 3)
+            return fail(NSC_ERR_INVALID_ARG,
+                        "%s: shift row %lld has column value %lld (0..3 expected)",
+                        op, (long long)s, (long long)iv);
         if (iv) st->inv[s >> 5] |= 1u << (s & 31);
-        if (iv == 2) {
+        if (iv >= 2) {
             st->per[s >> 5] |= 1u << (s & 31);
             st->any_per = 1;
+        }
+        if (iv == 3) {
+            st->nofwd[s >> 5] |= 1u << (s & 31);
+            st->any_tr = 1;
         }
         const int32_t a = static_cast<int32_t>(dx < 0 ? -dx : dx);
         const int32_t b = static_cast<int32_t>(dy < 0 ? -dy : dy);

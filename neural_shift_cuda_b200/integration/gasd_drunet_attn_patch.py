@@ -15,9 +15,12 @@ Patched methods (CUDA inputs, `use_cuda_shift` on):
 * `forward_cached(x, cache)`, `_KT_action_cached`, `laplacian_grw_cached`
   for a fixed guide's cached edges (`cache.shifts`, `cache.w_list`,
   `cache.Z`, `cache.C`).
-* `_KT_action`, `NLM_transpose`, `laplacian_grw`: K^T through the identity
-  pi^-1(w * y) = pi^-1(w) * pi^-1(y): the weights rolled back by their own
-  shift and the negated table.
+* `_KT_action`, `NLM_transpose`, `laplacian_grw`: K^T y(p) =
+  sum_s w_s(p - d) y(p - d), one `accumulate_uz(..., transpose=True)` over
+  the forward weight stack itself.  (The reference rolls every weight plane
+  by its shift into a second stack and accumulates over the negated table,
+  pi^-1(w * y) = pi^-1(w) * pi^-1(y); the kernel reads the planes at
+  p - d instead, so no rolled copy is made.)
 
 A single-head model's weights stay one-channel (the kernels share them
 across channels) instead of being expanded and copied C times.
@@ -34,7 +37,7 @@ from torch.utils.checkpoint import checkpoint as grad_checkpoint
 
 from ..ops import accumulate_uz, normalized_accumulate_uz, shift_gather
 from ._common import (box_stack, cached_shift_tensor, flat, head_mix_matrix,
-                      mix_heads, normalise_sigma, roll_slices, shift_tensor)
+                      mix_heads, normalise_sigma, shift_tensor)
 
 
 def _rows(model):
@@ -43,12 +46,6 @@ def _rows(model):
 
 def _get_shift_tensor(self, device):
     return cached_shift_tensor(self, "_nsc_gasd_shifts", lambda: _rows(self), device)
-
-
-def _kt_shifts(model, device):
-    return cached_shift_tensor(
-        model, "_nsc_gasd_kt_shifts",
-        lambda: [(-dx, -dy, 0) for dx, dy, _ in _rows(model)], device)
 
 
 def _eval_chunking(model):
@@ -140,19 +137,7 @@ def _pack(self, x, cache):
     stack = torch.stack(w, 0)
     shifts = shift_tensor([(dx, dy, 0) for dx, dy in cache.shifts], x.device)
     self._nsc_gasd_pack = (cache, key, stack, shifts)
-    self._nsc_gasd_pack_t = None
     return stack, shifts
-
-
-def _pack_t(self, x, cache):
-    stack, shifts = _pack(self, x, cache)
-    st = getattr(self, "_nsc_gasd_pack_t", None)
-    if st is not None and st[0] is cache:
-        return st[1], st[2]
-    w_t = flat(roll_slices(stack, shifts[:, :2], 1))
-    kt = torch.stack([-shifts[:, 0], -shifts[:, 1], shifts[:, 2]], 1).contiguous()
-    self._nsc_gasd_pack_t = (cache, w_t, kt)
-    return w_t, kt
 
 
 def _forward_cached_cuda(self, x, cache, return_D=True):
@@ -164,8 +149,8 @@ def _forward_cached_cuda(self, x, cache, return_D=True):
 
 
 def _kt_action_cached_cuda(self, y, cache):
-    w_t, kt = _pack_t(self, y, cache)
-    return accumulate_uz(y.contiguous(), w_t, kt)[0]
+    stack, shifts = _pack(self, y, cache)
+    return accumulate_uz(y.contiguous(), flat(stack), shifts, transpose=True)[0]
 
 
 def _lap_from(z, log_Z):
@@ -183,17 +168,16 @@ def _laplacian_grw_cached_cuda(self, x, cache, eps=1e-10):
 
 # ------------------------------------------------------------- transpose
 
-def _transpose_inputs(self, x, guide, sig):
-    w = _weight_stack(self, x, guide, sig)
-    shifts = _get_shift_tensor(self, x.device)
-    return w, flat(roll_slices(w, shifts[:, :2], 1)), _kt_shifts(self, x.device)
+def _kt(self, y, w_flat):
+    """K^T y over the flat forward stack."""
+    return accumulate_uz(y.contiguous(), w_flat, _get_shift_tensor(self, y.device),
+                         transpose=True)[0]
 
 
 def _kt_action_cuda(self, y, guide=None, sig=None):
     _eval_chunking(self)
     sig = normalise_sigma(y, sig)
-    _, w_t, kt = _transpose_inputs(self, y, guide, sig)
-    out = accumulate_uz(y.contiguous(), w_t, kt)[0]
+    out = _kt(self, y, flat(_weight_stack(self, y, guide, sig)))
     _restore_chunking(self)
     return out
 
@@ -201,9 +185,9 @@ def _kt_action_cuda(self, y, guide=None, sig=None):
 def _nlm_transpose_cuda(self, x, guide=None, sig=None, return_D=False):
     _eval_chunking(self)
     sig = normalise_sigma(x, sig)
-    w, w_t, kt = _transpose_inputs(self, x, x if guide is None else guide, sig)
+    w = _weight_stack(self, x, x if guide is None else guide, sig)
     D = w.sum(0).expand(x.shape)
-    out = accumulate_uz((x / D.clamp_min(1e-6)).contiguous(), w_t, kt)[0]
+    out = _kt(self, x / D.clamp_min(1e-6), flat(w))
     _restore_chunking(self)
     return (out, D) if return_D else (out, None)
 
@@ -211,12 +195,12 @@ def _nlm_transpose_cuda(self, x, guide=None, sig=None, return_D=False):
 def _laplacian_grw_cuda(self, x, guide, sig=None, eps=1e-10):
     _eval_chunking(self)
     sig = normalise_sigma(x, sig)
-    w, w_t, kt = _transpose_inputs(self, x, x if guide is None else guide, sig)
+    w = flat(_weight_stack(self, x, x if guide is None else guide, sig))
     D, log_Z = normalized_accumulate_uz(
-        x.contiguous(), flat(w), _get_shift_tensor(self, x.device),
+        x.contiguous(), w, _get_shift_tensor(self, x.device),
         return_log_degree=True, validate=False)
     z = x - D
-    out = z - accumulate_uz(_lap_from(z, log_Z).contiguous(), w_t, kt)[0]
+    out = z - _kt(self, _lap_from(z, log_Z), w)
     _restore_chunking(self)
     return out
 

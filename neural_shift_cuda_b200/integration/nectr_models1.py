@@ -1,12 +1,15 @@
-"""NECTR model 1, restated for testing -- TEST INFRASTRUCTURE ONLY.
+"""The NECTR model-1 architecture (`NECTR_denoiser`), the class the NECTR
+installer patches.
 
 A restatement of `models/NECTR_models1.py` of the reference checkout
-(`NECTR_denoiser`, lines 12-244): the feature network (`pre_activation`,
-:84-116), the pairwise weight head (`N_theta`, :118-148) and the serial
-per-shift forward (:154-244), which is the end-to-end oracle of the
-NECTR benchmark configuration.  Parameter names follow the reference so
-its state dicts load unchanged; `tests/golden/make_golden.py` stores the
-reference model's own outputs for seeded inputs and
+(lines 12-244): the feature network (`pre_activation`, :84-116), the
+pairwise weight head (`N_theta`, :118-148) and the serial per-shift forward
+(:154-244).  It is not part of the kernel path: the package ships it so the
+NECTR forward can be benchmarked (random init, the benchmark's shapes) and
+tested without the reference checkout.  Its serial `forward` is the
+end-to-end check of the installed forward.  Parameter names follow the
+reference so its state dicts load unchanged; `tests/golden/make_golden.py`
+stores the reference model's own outputs for seeded inputs and
 `tests/test_oracle_golden.py` pins this restatement to them.
 """
 

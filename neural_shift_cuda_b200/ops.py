@@ -256,9 +256,11 @@ class _AccumulateUZFn(torch.autograd.Function):
         return gx.to(x.dtype), gw, None
 
 
-def _prep_reduction(x, weights, shifts, op, periodic_mirror=False):
+def _prep_reduction(x, weights, shifts, op, periodic_mirror=False,
+                    transpose=False):
     xd, wd = _storage_dtypes(x, weights)
-    hs = _lib.mirror_mode(_check_shift_shape(shifts, True, op), periodic_mirror)
+    hs = _lib.mirror_mode(_check_shift_shape(shifts, not transpose, op),
+                          periodic_mirror, transpose)
     _require_cuda(op, x, weights)
     _check_nchw(x, "x")
     B, C, H, W = x.shape
@@ -269,16 +271,23 @@ def _prep_reduction(x, weights, shifts, op, periodic_mirror=False):
 
 
 def accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts, *,
-                  periodic_mirror: bool = False):
+                  periodic_mirror: bool = False, transpose: bool = False):
     """(U_num, Z) over all shifts including the mirror branch of has_inv
     rows; weights are pre-multiplied by the forward box mask by the caller
     (reference `ops.py:612-631`).  U = U_num / Z is left to the caller.
 
     periodic_mirror=True (an extension): the mirror term of every has_inv
     row reads w and x at (p - d) mod (H, W) without the inside test -- the
-    periodic (comp_box off) operator, without materialising rolled planes."""
+    periodic (comp_box off) operator, without materialising rolled planes.
+
+    transpose=True (an extension): the transpose of the forward-only
+    operator of the same (forward-only, (S, 2) or has_inv == 0) table and
+    weights, U(p) = sum_s w_s(p - d) x(p - d) circularly, Z likewise.  The
+    reference forms K^T as accumulate_uz over negated shifts and weight
+    planes rolled by (dx, dy) (`integration/gasd_drunet_attn_patch.py:494-549`);
+    this reads the original planes instead of a rolled copy."""
     x_k, w_k, hs = _prep_reduction(x, weights, shifts, "accumulate_uz",
-                                   periodic_mirror)
+                                   periodic_mirror, transpose)
     return _AccumulateUZFn.apply(x_k, w_k, hs)
 
 

@@ -189,10 +189,11 @@ def accumulate_uz(x: torch.Tensor, weights: torch.Tensor, shifts):
     u_terms, z_terms = [], []
     for s, (dx, dy, inv) in enumerate(rows):
         wf = wv[s]
-        u_terms.append(wf * _gather(x, dx, dy))
-        z_terms.append(wf)
+        if inv != 3:       # column value 3: transposed row, no forward term
+            u_terms.append(wf * _gather(x, dx, dy))
+            z_terms.append(wf)
         if inv:
-            wi = _mirror(wf, dx, dy, inv == 2)
+            wi = _mirror(wf, dx, dy, inv in (2, 3))
             u_terms.append(wi * _gather(x, -dx, -dy))
             z_terms.append(wi)
     return tree_sum(torch.stack(u_terms)), tree_sum(torch.stack(z_terms))
@@ -218,10 +219,13 @@ def accumulate_uz_backward(x, weights, grad_U, grad_Z, shifts):
     gws = []
     for s, (dx, dy, inv) in enumerate(rows):
         wf = wv[s]
-        gx = gx + _gather(wf * gU, -dx, -dy)
-        gw = _gather(x, dx, dy) * gU + gZ
+        if inv != 3:
+            gx = gx + _gather(wf * gU, -dx, -dy)
+            gw = _gather(x, dx, dy) * gU + gZ
+        else:
+            gw = torch.zeros_like(x)
         if inv:
-            m = box_mask(H, W, dx, dy, dt) if inv != 2 else torch.ones(H, W, dtype=dt)
+            m = box_mask(H, W, dx, dy, dt) if inv not in (2, 3) else torch.ones(H, W, dtype=dt)
             gx = gx + m * wf * _gather(gU, dx, dy)
             gw = gw + m * (x * _gather(gU, dx, dy) + _gather(gZ, dx, dy))
         if Cw == 1 and C > 1:

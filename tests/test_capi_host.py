@@ -143,3 +143,17 @@ def test_host_shift_cache_roundtrip():
     assert hs2.rows() == [(1, -2, 1), (0, 0, 0)]
     assert _lib.host_shifts(torch.tensor([[1, -2, 1]], dtype=torch.int32)).t.dtype \
         == torch.int64
+
+
+def test_transposed_rows_only_for_accumulate():
+    """Column value 3 (transposed row) is an accumulate_uz table value; the
+    normalized entry point rejects it before any launch, and values outside
+    0..3 are rejected everywhere."""
+    t, p = _shift_arr([[0, 1, 3], [1, 0, 3]])
+    st, msg = _status("nsc_normalized_accumulate_uz_fwd", None, 2, None, 2, 1, 1,
+                      1, 4, 4, p, 2, 1, None, None, None, None)
+    assert st != 0 and "accumulate_uz only" in msg
+    t, p = _shift_arr([[0, 1, 5]])
+    st, msg = _status("nsc_accumulate_uz_fwd", None, 2, None, 2, 1, 1, 1, 4, 4,
+                      p, 1, None, None, None)
+    assert st != 0 and "0..3 expected" in msg

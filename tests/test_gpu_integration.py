@@ -24,7 +24,7 @@ import torch.nn.functional as F
 
 from neural_shift_cuda_b200 import integration as I
 from oracle import nsc_oracle as O
-from oracle.nectr_model import NECTR_denoiser
+from neural_shift_cuda_b200.integration.nectr_models1 import NECTR_denoiser
 import stub_models as SM
 
 pytestmark = pytest.mark.gpu

@@ -94,3 +94,37 @@ def test_value_two_without_flag_is_masked(cuda):
     Ur, Zr = O.accumulate_uz(x, w, rows)
     close(U, Ur, 1e-12)
     close(Z, Zr, 1e-12)
+
+
+@pytest.mark.parametrize("C,Cw", [(3, 1), (3, 3), (5, 1)])
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-11), (torch.float32, 1e-5)])
+def test_accumulate_transpose_fwd_bwd(cuda, C, Cw, dtype, tol):
+    """accumulate_uz(..., transpose=True): U(p) = sum_s w_s(p - d) x(p - d)
+    over the original planes, against the oracle's transposed rows (pinned
+    to the reference's rolled-plane K^T form on the CPU)."""
+    torch.manual_seed(4)
+    B, H, W, R = 2, 11, 14, 2
+    rows = O.window_shifts(R)
+    S = len(rows)
+    x = torch.rand(B, C, H, W, dtype=dtype)
+    w = torch.rand(S * B, Cw, H, W, dtype=dtype)
+    xc = x.to(cuda).requires_grad_(True)
+    wc = w.to(cuda).requires_grad_(True)
+    sh = torch.tensor([(dx, dy) for dx, dy, _ in rows])
+    U, Z = nsc.accumulate_uz(xc, wc, sh, transpose=True)
+    tr = [(dx, dy, 3) for dx, dy, _ in rows]
+    Ur, Zr = O.accumulate_uz(x, w.expand(-1, C, -1, -1), tr)
+    close(U, Ur, tol)
+    close(Z, Zr, tol)
+    gU, gZ = torch.randn_like(Ur), torch.randn_like(Zr)
+    (U * gU.to(cuda) + Z * gZ.to(cuda)).sum().backward()
+    gx, gw = O.accumulate_uz_backward(x, w, gU, gZ, tr)
+    close(xc.grad, gx, tol)
+    close(wc.grad, gw, tol)
+
+
+def test_transpose_rejects_mirror_rows(cuda):
+    x = torch.rand(1, 1, 6, 6, device=cuda)
+    w = torch.rand(3, 1, 6, 6, device=cuda)
+    with pytest.raises(ValueError, match="forward-only"):
+        nsc.accumulate_uz(x, w, torch.tensor(O.halfplane_shifts(1))[:3], transpose=True)

@@ -106,7 +106,7 @@ def test_nectr_model_restatement(act):
     """The restated NECTR model 1 reproduces the reference model's serial
     forward on the stored weights."""
     from types import SimpleNamespace
-    from oracle.nectr_model import NECTR_denoiser
+    from neural_shift_cuda_b200.integration.nectr_models1 import NECTR_denoiser
     c = GOLD_NECTR[act]
     m = NECTR_denoiser(SimpleNamespace(**c["args"])).double()
     m.load_state_dict(c["state"])

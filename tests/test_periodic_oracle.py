@@ -91,3 +91,36 @@ def test_normalized_backward_periodic_equals_explicit_edges():
             k += 1
         fold.append(g)
     torch.testing.assert_close(gw, torch.cat(fold, 0), rtol=1e-12, atol=1e-12)
+
+
+def test_accumulate_transposed_rows_equal_rolled_kt():
+    """Column value 3 (transposed row): sum_s w_s(p - d) x(p - d) equals the
+    reference's K^T form -- accumulate over the negated shifts with every
+    weight plane rolled by its own (dx, dy)
+    (`integration/gasd_drunet_attn_patch.py:494-549`) -- values and
+    gradients."""
+    torch.manual_seed(1)
+    B, C, H, W, R = 2, 3, 8, 10, 2
+    rows = O.window_shifts(R)
+    S = len(rows)
+    x = torch.rand(B, C, H, W, dtype=torch.float64)
+    w = torch.rand(S * B, 1, H, W, dtype=torch.float64)
+    tr = [(dx, dy, 3) for dx, dy, _ in rows]
+    U, Z = O.accumulate_uz(x, w.expand(-1, C, -1, -1), tr)
+
+    def rolled(wt):
+        ws = wt.reshape(S, B, *wt.shape[1:])
+        return torch.cat([torch.roll(ws[s], shifts=(dx, dy), dims=(-2, -1))
+                          for s, (dx, dy, _) in enumerate(rows)], 0)
+    neg = [(-dx, -dy, 0) for dx, dy, _ in rows]
+    Uk, Zk = O.accumulate_uz(x, rolled(w).expand(-1, C, -1, -1), neg)
+    torch.testing.assert_close(U, Uk, rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(Z, Zk, rtol=1e-12, atol=1e-12)
+    gU, gZ = torch.randn_like(U), torch.randn_like(Z)
+    gx, gw = O.accumulate_uz_backward(x, w, gU, gZ, tr)
+    wv = w.clone().requires_grad_(True)
+    xv = x.clone().requires_grad_(True)
+    U2, Z2 = O.accumulate_uz(xv, rolled(wv).expand(-1, C, -1, -1), neg)
+    (U2 * gU + Z2 * gZ).sum().backward()
+    torch.testing.assert_close(gx, xv.grad, rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(gw, wv.grad, rtol=1e-12, atol=1e-12)
