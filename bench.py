@@ -557,7 +557,7 @@ def _nectr_model(dev, dtype):
     return m.to(device=dev, dtype=dtype).eval()
 
 
-def _wl_nectr(dtype_name):
+def _wl_nectr(dtype_name, fused=True):
     Bt, Hs, Ws, Rr = 8, 256, 256, 5
     rows = halfplane(Rr)
     Sn = len(rows)
@@ -570,6 +570,7 @@ def _wl_nectr(dtype_name):
     def make(dev, b0, nb):
         from neural_shift_cuda_b200.integration import nectr_patch as NP
         m = _nectr_model(dev, dtype)
+        m.use_nectr_fused = fused
         x = _seeded((1, Hs, Ws), b0, nb, 7, dev,
                     lambda g, sh: noisy(g, sh, dev)).to(dtype)
 
@@ -580,7 +581,8 @@ def _wl_nectr(dtype_name):
         def per_kernel(xi):
             """One forward with CUDA events around the two kernels of the
             path (pair_gather, normalized_accumulate_uz): median of 5."""
-            names = {"pair_gather": [], "normalized_accumulate_uz": []}
+            names = ({"_forward_fused": []} if fused else
+                     {"pair_gather": [], "normalized_accumulate_uz": []})
             sizes = {}
             orig = {k: getattr(NP, k) for k in names}
 
@@ -595,6 +597,11 @@ def _wl_nectr(dtype_name):
                     names[k].append((e0, e1))
                     sizes[k] = _nbytes([t for t in a if isinstance(t, torch.Tensor)]
                                        ) + _nbytes(out)
+                    if k == "_forward_fused":
+                        # x and the guide in; the two per-pixel maps written
+                        # and read once; D and Z out
+                        L1 = m.proj[0][0].out_channels
+                        sizes[k] += 2 * 2 * a[2].shape[0] * L1 * Hs * Ws * 4
                     return out
                 return f
             try:
@@ -616,9 +623,9 @@ def _wl_nectr(dtype_name):
             # reduction counts x, the (S*B, 1, H, W) values, D and log_C.
             return res
 
-        return dict(inputs=[x], run=run, launches=2,
+        return dict(inputs=[x], run=run, launches=1 if fused else 2,
                     units=Sn * nb * 1 * Hs * Ws, per_kernel=per_kernel,
-                    dominant="pair_gather")
+                    dominant="_forward_fused" if fused else "pair_gather")
 
     def cpu(nb):
         dev = torch.device("cpu")
@@ -633,11 +640,14 @@ def _wl_nectr(dtype_name):
                 f"per-shift loop) on 1 of {Bt} images, fp32, torch CPU")
 
     return OpWorkload(
-        "nectr_" + dtype_name,
+        "nectr_" + dtype_name + ("" if fused else "_unfused"),
         f"pixel-shifts/s (NECTR model-1 patched forward, configs[1]: x "
         f"(8,1,256,256) {dtype_name}, latent 16, R=5 S=61)", Bt,
-        {"workload": f"NECTR_models1 patched forward (pair_gather -> weight "
-                     f"head -> normalized_accumulate_uz, log mode), x "
+        {"workload": f"NECTR_models1 patched forward ("
+                     + ("fused pair gather + weight head + normalized "
+                        "accumulation, one kernel" if fused else
+                        "pair_gather -> weight head -> normalized_accumulate_uz")
+                     + f", log mode), x "
                      f"(8,1,256,256) {dtype_name} U[0,1]+N(0,(25/255)^2), "
                      f"concat, residual_depth 2, proj_depth 1, latent 16, "
                      f"R=5 S=61, random init (configs[1])",
@@ -648,7 +658,9 @@ def _wl_nectr(dtype_name):
 WORKLOADS = {"pair_gather": _wl_pair_gather, "normalized": _wl_normalized,
              "metropolis": _wl_metropolis,
              "nectr": lambda: _wl_nectr("f32"),
-             "nectr_bf16": lambda: _wl_nectr("bf16")}
+             "nectr_bf16": lambda: _wl_nectr("bf16"),
+             "nectr_unfused": lambda: _wl_nectr("f32", fused=False),
+             "nectr_bf16_unfused": lambda: _wl_nectr("bf16", fused=False)}
 
 
 def _nbytes(ts):
@@ -738,7 +750,7 @@ def run_workload(args, wl):
         dist.all_reduce(u)
         units_all = u.item()
     step_ms = [a.elapsed_time(b) for a, b in ev]
-    kern_ms = statistics.median(step_ms)
+    step_median = kern_ms = statistics.median(step_ms)
     alg = _nbytes(inputs) + _nbytes(out)
     kernels = None
     roof_note = "step time of all launches of the op (per rank)"
@@ -829,7 +841,7 @@ def run_workload(args, wl):
             "kernels": kernels,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": w["launches"] * args.steps,
-            "step_ms": {"min": min(step_ms), "median": kern_ms, "max": max(step_ms)},
+            "step_ms": {"min": min(step_ms), "median": step_median, "max": max(step_ms)},
             "clocks": clocks}), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -196,6 +196,41 @@ NSC_API nsc_status nsc_normalized_accumulate_uz_bwd(
     const void* grad_log_C, void* grad_x, void* grad_w, void* stream);
 
 /* ---------------------------------------------------------------------
+ * NECTR model-1 patched forward, fused.  Replaces the pair_gather ->
+ * weight head -> normalized_accumulate_uz sequence of the reference's
+ * NECTR installer (neural_shift_cuda/integration/nectr_patch.py:214-234,
+ * ops pair_gather and normalized_accumulate_uz) for inference, without the
+ * (S*B, 2L, H, W) pair batch.  The first 1x1 convolution of the head,
+ * W1 [g(p); g(p+d)] + b1, is passed split: AB_map (B, 2 width, H, W) holds
+ * W1[:, :L] g in channels [0, width) and W1[:, L:] g in [width, 2 width);
+ * it is in `dtype` (fp32 or fp64), as is x (B, C, H, W), C in {1, 3}.
+ * `params` (host, `n_params` doubles): b1[width]; LayerNorm-1 gamma[width],
+ * beta[width]; for depth 2 also W2[width/2][width], b2[width/2],
+ * LayerNorm-2 gamma, beta [width/2]; then the output convolution
+ * Wout[cout][last width] (no bias), cout = C (mode 0, 1) or 3C (mode 2:
+ * chunks k, a, b).  width in {8, 16, 32}, depth in {1, 2}, LeakyReLU
+ * slope in [0, 1].
+ * mode 1: exp head, logits v * inv_sigma2 (log weights); mode 2:
+ * controlled sigmoid softplus(a) / (1 + exp(-sigmoid(b) k)) + 1e-8
+ * (positive weights); mode 0: raw v with plain sums.  Forward keys are
+ * masked by the box (p + d inside), mirror keys (has_inv rows) by p - d
+ * inside.  out0/out1: D and log_C (modes 1, 2) or U and Z (mode 0),
+ * (B, C, H, W) in `dtype`; `invalid_flag` (device int, may be NULL) is
+ * OR-ed with 1 when a key is NaN / +inf (negative in mode 2).  Radius
+ * <= 16 and (2 width + C)(8 + 2R)(32 + 2R) elements must fit in 227 KB of
+ * shared memory.  No backward: the installer uses it when autograd is off.
+ * ------------------------------------------------------------------- */
+NSC_API nsc_status nsc_nectr_fused_fwd(const void* x, const void* AB_map,
+                               int dtype, int64_t B,
+                               int64_t C, int64_t H, int64_t W,
+                               int64_t width, int depth,
+                               const double* params, int64_t n_params,
+                               double ln_eps1, double ln_eps2, double slope,
+                               double inv_sigma2, const int64_t* shifts,
+                               int64_t S, int mode, void* out0, void* out1,
+                               int* invalid_flag, void* stream);
+
+/* ---------------------------------------------------------------------
  * metropolis_aggregate.  Replaces `_C.metropolis_aggregate`
  * (csrc/metropolis.cpp:29-37, metropolis_cuda.cu:195-240) and adds the
  * backward the reference lacks.  w_half: (B, S, w_channels, H, W);

@@ -66,6 +66,9 @@ _SIGS = {
                                    _L, _I, _D, _P, _P, _P],
     "nsc_metropolis_bwd": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP, _L, _I,
                            _D, _P, _P, _P, _P, _P, _P, _P, _P],
+    "nsc_nectr_fused_fwd": [_P, _P, _I, _L, _L, _L, _L, _L, _I,
+                            ctypes.POINTER(ctypes.c_double), _L, _D, _D, _D, _D,
+                            _LP, _L, _I, _P, _P, _P, _P],
 }
 
 EXPORTED = ["nsc_index_width_bits", "nsc_version", "nsc_last_error_string",

@@ -15,6 +15,16 @@ exponential head is kept in log space (`value / sigma^2`) so the positive
 activation can never overflow before normalisation.  The official API
 returns `(U / Z, Z)`; Z is materialised in float64 from log_C.
 
+Fused inference path (no counterpart in the reference): when autograd is
+off, no weight cache is read or stored and the head is the model-1
+`proj` stack (1x1 conv, channel LayerNorm, LeakyReLU; one or two blocks of
+width 8 / 16 / 32) followed by the bias-free `out` conv, the whole
+sequence above runs as ONE kernel (`nsc_nectr_fused_fwd`): the first conv
+of [g(p); g(p+d)] is split into two per-pixel maps computed once, and the
+per-shift head is evaluated in registers, so the (S*B, 2L, H, W) pair batch
+(4 GB at the benchmark's shape) is never written.  `instance.use_nectr_fused
+= False` selects the unfused path.
+
 Differences from the reference installer: a CPU input runs the model's
 own original forward (the reference routes CPU inputs through its ops' CPU
 implementations); `instance.use_cuda_shift = False` also selects the
@@ -23,13 +33,16 @@ original forward.
 
 from __future__ import annotations
 
+import ctypes
 import functools
 import inspect
 from typing import List, Tuple
 
 import torch
 
-from ..ops import accumulate_uz, normalized_accumulate_uz, pair_gather, shift_gather
+from .. import _lib
+from ..ops import (_defer_flag, accumulate_uz, check_validation,
+                   normalized_accumulate_uz, pair_gather, shift_gather)
 from ._common import halfplane_rows, shift_tensor
 
 _MISSING = object()
@@ -154,10 +167,107 @@ def _aggregate(x, values, shifts, kind):
     return U / Z, Z
 
 
+def _fused_head(model, x):
+    """(width, depth, params, eps1, eps2, slope, mode) of a head the fused
+    kernel implements, or None."""
+    if not getattr(model, "use_nectr_fused", True) or _is_model2(model):
+        return None
+    if getattr(model, "model_type", "concat") != "concat":
+        return None
+    act = model.output_activation
+    mode = {"exp": 1, "control_sigmoid": 2}.get(act, 0)
+    if act == "sig":
+        return None
+    proj, out = getattr(model, "proj", None), getattr(model, "out", None)
+    if proj is None or out is None or not 1 <= len(proj) <= 2:
+        return None
+    C = x.shape[1]
+    if C not in (1, 3) or not isinstance(out, torch.nn.Conv2d) or out.bias is not None:
+        return None
+    convs, norms, slopes = [], [], set()
+    for blk in proj:
+        if len(blk) != 3:
+            return None
+        cv, ln, act_l = blk
+        if not (isinstance(cv, torch.nn.Conv2d) and cv.kernel_size == (1, 1)
+                and cv.bias is not None and isinstance(ln, torch.nn.LayerNorm)
+                and ln.elementwise_affine and isinstance(act_l, torch.nn.LeakyReLU)):
+            return None
+        convs.append(cv)
+        norms.append(ln)
+        slopes.add(float(act_l.negative_slope))
+    width = convs[0].out_channels
+    if width not in (8, 16, 32) or len(slopes) != 1 or not 0.0 <= min(slopes) <= 1.0:
+        return None
+    if len(proj) == 2 and (convs[1].in_channels != width
+                           or convs[1].out_channels != width // 2):
+        return None
+    cout = C * (3 if mode == 2 else 1)
+    if out.out_channels != cout or out.in_channels != convs[-1].out_channels:
+        return None
+    R = max(max(abs(dx), abs(dy)) for dx, dy, _ in _rows(model))
+    es = 8 if x.dtype == torch.float64 else 4
+    if R > 16 or (2 * width + C) * (8 + 2 * R) * (32 + 2 * R) * es > 227 * 1024:
+        return None
+    flat = [convs[0].bias, norms[0].weight, norms[0].bias]
+    if len(proj) == 2:
+        flat += [convs[1].weight[:, :, 0, 0], convs[1].bias, norms[1].weight,
+                 norms[1].bias]
+    flat.append(out.weight[:, :, 0, 0])
+    # host copy of the head parameters, refreshed only when one changes
+    key = tuple((t.data_ptr(), t._version) for t in flat)
+    held = getattr(model, "_nsc_fused_params", None)
+    if held is None or held[0] != key:
+        params = torch.cat([t.detach().reshape(-1).to(torch.float64).cpu()
+                            for t in flat]).contiguous()
+        held = (key, params)
+        model._nsc_fused_params = held
+    params = held[1]
+    return (width, len(proj), params, float(norms[0].eps),
+            float(norms[-1].eps), slopes.pop(), mode)
+
+
+def _forward_fused(model, x, guide, head, shifts):
+    width, depth, params, eps1, eps2, slope, mode = head
+    dt = torch.float64 if x.dtype == torch.float64 else torch.float32
+    g = guide.to(dt)
+    L = g.shape[1]
+    W1 = model.proj[0][0].weight.detach().to(dt)[:, :, 0, 0]
+    if W1.shape[1] != 2 * L:
+        return None
+    B, _, H, W = guide.shape
+    # [W1[:, :L]; W1[:, L:]] g as one batched product: (B, 2 width, H*W)
+    AB = torch.matmul(torch.cat([W1[:, :L], W1[:, L:]], 0), g.reshape(B, L, H * W))
+    xk = x.to(dt).contiguous()
+    C = xk.shape[1]
+    o0 = torch.empty_like(xk)
+    o1 = torch.empty_like(xk)
+    flag = torch.zeros(1, dtype=torch.int32, device=x.device) if mode else None
+    hs = _lib.host_shifts(shifts)
+    with torch.cuda.device(x.device):
+        _lib.call("nsc_nectr_fused_fwd", _lib.ptr(xk), _lib.ptr(AB),
+                  _lib.dtype_code(dt), B, C, H, W, width, depth,
+                  ctypes.cast(params.data_ptr(), ctypes.POINTER(ctypes.c_double)),
+                  params.numel(), eps1, eps2, slope, 1.0 / float(model.sigma) ** 2,
+                  hs.ptr, hs.S, mode, _lib.ptr(o0), _lib.ptr(o1), _lib.ptr(flag),
+                  _lib.stream_of(xk))
+    if mode == 0:
+        return o0 / o1, o1
+    _defer_flag(flag, mode == 1)
+    return o0, o1.to(torch.float64).exp()
+
+
 def _forward_official(model, x, reference=None, sig=None, cache=None,
                       store_cache=False):
     guide = model.pre_activation(x if reference is None else reference, sigma=sig)
     rows, shifts = _shifts(model, x.device)
+    if cache is None and not store_cache and not torch.is_grad_enabled():
+        head = _fused_head(model, x)
+        if head is not None:
+            check_validation(block=False)
+            out = _forward_fused(model, x, guide, head, shifts)
+            if out is not None:
+                return out
     if cache is None:
         values, kind = _weights(model, guide, shifts)
         held = _to_cache(values, rows, x.shape[0], kind) if store_cache else None

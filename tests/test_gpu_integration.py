@@ -37,6 +37,16 @@ _INSTALL = {"gasd": I.install_cuda_shift_gasd, "nekde": I.install_cuda_shift_att
             "nkd": I.install_cuda_shift_metropolis}
 
 
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    """fp32 convolutions in full fp32 (cuDNN defaults to TF32, ~1e-3
+    relative), so fp32 results can be held to fp32 tolerances."""
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cudnn.allow_tf32 = prev
+
+
 def _roll(x, dx, dy):
     """gather convention: out(h, w) = x(h+dx, w+dy) circularly"""
     return torch.roll(x, shifts=(-dx, -dy), dims=(-2, -1))
@@ -82,15 +92,22 @@ def test_nectr_fp32_and_bf16_inputs(cuda):
          + (25 / 255) * torch.randn(2, 1, 40, 48, generator=g)).to(cuda)
     with torch.no_grad():
         U, Z = m(x)
-        m.use_cuda_shift = False
-        Us, Zs = m(x)
-        m.use_cuda_shift = True
+        m.use_nectr_fused = False
+        Uu, Zu = m(x)                  # unfused: pair batch + ops
+        m.use_nectr_fused = True
+        md = cls(args).to(cuda)
+        md.load_state_dict(m.state_dict())
+        md = md.double()
+        md.use_cuda_shift = False
+        Us, Zs = md(x.double())        # serial forward in fp64
         mb = m.bfloat16()
         Ub, _ = mb(x.bfloat16())
-    torch.testing.assert_close(U, Us, rtol=1e-4, atol=1e-5)
-    torch.testing.assert_close(Z.float(), Zs, rtol=1e-4, atol=1e-5)
+    # fp32 (fused and unfused) against the fp64 serial forward
+    for u, z in ((U, Z), (Uu, Zu)):
+        torch.testing.assert_close(u.double(), Us, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(z.double(), Zs.double(), rtol=1e-4, atol=1e-5)
     assert Ub.dtype == torch.float32
-    assert (Ub - Us).abs().max() < 0.1   # bf16 weight head
+    assert (Ub.double() - Us).abs().max() < 0.1   # bf16 weight head
 
 
 # ------------------------------------------------------------ stub models
@@ -277,3 +294,78 @@ def test_installers_match_reference_installers(cuda, name):
             _close(Wx, c["Wx"])
             _close(dh, c["d_hat"])
             _close(m(x, guide=guide)[0], c["Wx_guided"])
+
+
+# ----------------------------------------------------- fused NECTR forward
+
+def _nectr(args_over, cuda, seed=0):
+    args = dict(model_type="concat", residual_depth=2, proj_depth=1, latent_dim=16,
+                patch_rad=1, output_activation="exp", window_rad=5, in_channel=1,
+                blind=True)
+    args.update(args_over)
+    cls = type("NECTRFused", (NECTR_denoiser,), {})
+    I.install_cuda_shift_nectr(cls)
+    torch.manual_seed(seed)
+    return cls(SimpleNamespace(**args)).to(cuda)
+
+
+@pytest.mark.parametrize("over", [
+    {},                                                      # benchmark head
+    {"output_activation": "control_sigmoid"},
+    {"output_activation": "none"},
+    {"proj_depth": 2, "latent_dim": 32, "window_rad": 3},
+    {"in_channel": 3, "latent_dim": 8, "window_rad": 2},
+    {"in_channel": 3, "output_activation": "control_sigmoid", "proj_depth": 2,
+     "latent_dim": 16, "window_rad": 4},
+])
+def test_nectr_fused_matches_fp64_serial(cuda, over):
+    """The fused kernel (fp32) against the model's own serial forward in
+    fp64 and against the unfused patched path (fp32)."""
+    m = _nectr(over, cuda)
+    C = m.in_channel
+    g = torch.Generator().manual_seed(1)
+    x = (torch.rand(2, C, 40, 48, generator=g)
+         + (25 / 255) * torch.randn(2, C, 40, 48, generator=g)).to(cuda)
+    with torch.no_grad():
+        D, Z = m(x)                                   # fused
+        m.use_nectr_fused = False
+        Du, Zu = m(x)                                 # pair batch + ops
+        m.use_nectr_fused = True
+        md = m.double()
+        md.use_cuda_shift = False
+        Ds, Zs = md(x.double())                       # serial, fp64
+        md.use_cuda_shift = True
+        Dd, Zd = md(x.double())                       # fused, fp64
+    torch.testing.assert_close(D.double(), Ds, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(Z.double(), Zs.double(), rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(D, Du, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(Dd, Ds, rtol=1e-9, atol=1e-10)
+    torch.testing.assert_close(Zd.double(), Zs.double(), rtol=1e-9, atol=1e-10)
+
+
+def test_nectr_fused_benchmark_shape(cuda):
+    """configs[1] shape: B = 8, 1 x 256 x 256, R = 5, latent 16, fp32 and a
+    bf16 model; fused against the fp64 serial forward."""
+    m = _nectr({}, cuda)
+    g = torch.Generator().manual_seed(0)
+    x = (torch.rand(8, 1, 256, 256, generator=g)
+         + (25 / 255) * torch.randn(8, 1, 256, 256, generator=g)).to(cuda)
+    with torch.no_grad():
+        D, Z = m(x)
+        md = _nectr({}, cuda).double()
+        md.use_cuda_shift = False
+        Ds, Zs = md(x.double())
+        mb = _nectr({}, cuda).bfloat16()
+        Db, _ = mb(x.bfloat16())
+    torch.testing.assert_close(D.double(), Ds, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(Z, Zs, rtol=1e-4, atol=1e-5)
+    assert Db.dtype == torch.float32
+    assert (Db.double() - Ds).abs().max() < 0.1   # bf16 head weights and inputs
+
+
+def test_nectr_fused_not_used_with_autograd(cuda):
+    m = _nectr({"window_rad": 2, "latent_dim": 8}, cuda)
+    x = torch.rand(1, 1, 16, 24, device=cuda)
+    D, Z = m(x)                       # grad enabled: differentiable path
+    D.sum().backward()
+    assert m.out.weight.grad is not None
