@@ -147,6 +147,23 @@ NSC_API nsc_status nsc_accumulate_uz_band_fwd(const void* x_ext, int x_dtype,
                                       const int64_t* shifts, int64_t S,
                                       void* U, void* Z, void* stream);
 
+/* nsc_accumulate_uz_band_fwd restricted to the band's output rows
+ * [r_begin, r_end) (other rows of U, Z are not written), with the
+ * persistent grid capped at max_ctas CTAs (0: one per SM).  No counterpart
+ * in the reference (which has no multi-GPU split): the interior rows
+ * [R, Hb - R) read no halo row, so they run while the halo exchange is in
+ * flight, on SMs left free for the collective; the 2R border rows follow
+ * the exchange. */
+NSC_API nsc_status nsc_accumulate_uz_band_rows_fwd(const void* x_ext, int x_dtype,
+                                           const void* w, int w_dtype,
+                                           int64_t w_channels, int64_t B,
+                                           int64_t C, int64_t Hb, int64_t W,
+                                           int64_t row0, int64_t Hg,
+                                           int64_t r_begin, int64_t r_end,
+                                           int max_ctas, const int64_t* shifts,
+                                           int64_t S, void* U, void* Z,
+                                           void* stream);
+
 /* Mirror contributions of this band's own weights to the R rows just
  * above (edge_top: global rows row0-R .. row0-1) and just below
  * (edge_bot: rows row0+Hb .. row0+Hb+R-1) the band.  edge_top / edge_bot

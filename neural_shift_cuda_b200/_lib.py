@@ -51,6 +51,8 @@ _SIGS = {
                               _P, _P, _P, _P, _P],
     "nsc_accumulate_uz_band_fwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _L,
                                    _L, _LP, _L, _P, _P, _P],
+    "nsc_accumulate_uz_band_rows_fwd": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _L,
+                                        _L, _L, _L, _I, _LP, _L, _P, _P, _P],
     "nsc_accumulate_uz_band_edges": [_P, _I, _P, _I, _L, _L, _L, _L, _L, _L,
                                      _L, _LP, _L, _P, _P, _P],
     "nsc_accumulate_uz_band_add_strips": [_P, _P, _I, _L, _L, _L, _L, _L, _P,

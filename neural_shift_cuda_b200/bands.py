@@ -20,7 +20,10 @@ identical to the unsplit op:
 
 The strips need only the rank's own rows, so they are computed first and
 both exchanges travel in ONE grouped send/recv (`batch_isend_irecv`, NCCL
-over NVLink for CUDA tensors) before the band forward.  With
+over NVLink for CUDA tensors).  On CUDA the exchange is split in two so it
+leaves the critical path: the x halo travels while the edge-strip kernel
+runs, and the strips (needed only by the final add) travel while the band
+forward runs on all SMs but a few left to NCCL's kernels.  With
 `padded=True` the caller's x buffer has R spare rows above and below the
 band and the halo is received straight into them (no band-sized copy per
 step).  The compute is injectable so the exchange logic runs on CPU `gloo`
@@ -107,6 +110,18 @@ def band_edges_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
     return top, bot
 
 
+def band_rows_cuda(x_ext, w_band, shifts, row0: int, Hg: int, r0: int, r1: int,
+                   U: torch.Tensor, Z: torch.Tensor, max_ctas: int = 0) -> None:
+    """Write rows [r0, r1) of the band's (U, Z) (see band_forward_cuda);
+    max_ctas > 0 caps the persistent kernel's grid."""
+    hs, R, B, C, Hb, W, xd, wd, x_k, w_k, acc = _band_args(x_ext, w_band, shifts)
+    with torch.cuda.device(x_ext.device):
+        _lib.call("nsc_accumulate_uz_band_rows_fwd", _lib.ptr(x_k), _lib.dtype_code(xd),
+                  _lib.ptr(w_k), _lib.dtype_code(wd), w_k.size(1), B, C, Hb, W,
+                  row0, Hg, r0, r1, int(max_ctas), hs.ptr, hs.S, _lib.ptr(U),
+                  _lib.ptr(Z), _lib.stream_of(x_ext))
+
+
 def band_compute_cuda(x_ext, w_band, shifts, row0: int, Hg: int):
     """(U, Z, top, bot) of one band on its GPU via the C ABI (forward and
     edge strips; see band_forward_cuda / band_edges_cuda)."""
@@ -175,48 +190,74 @@ def exchange_halo_and_strips(x_pad: torch.Tensor, R: int, top, bot, group=None):
     and [R + Hb, Hb + 2R), band rows in between) from the ring neighbours,
     sends this band's mirror strips and returns the neighbours' strips
     (from_below, from_above), None at the image edges."""
+    return exchange_start(x_pad, R, top, bot, group)()
+
+
+def exchange_start(x_pad: torch.Tensor, R: int, top, bot, group=None,
+                   halo: bool = True, strips: bool = True):
+    """Issue the grouped send/recv of `exchange_halo_and_strips` -- the x
+    halo, the mirror strips or both -- and return a `finish()` that waits
+    for it (the current stream waits on the collective), writes the halo
+    rows into x_pad and returns (from_below, from_above)."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     Hb = x_pad.shape[2] - 2 * R
     if world == 1:
-        if R:
-            x_pad[:, :, :R] = x_pad[:, :, Hb:Hb + R]
-            x_pad[:, :, R + Hb:] = x_pad[:, :, R:2 * R]
-        return None, None
+        def finish_local():
+            if R and halo:
+                x_pad[:, :, :R] = x_pad[:, :, Hb:Hb + R]
+                x_pad[:, :, R + Hb:] = x_pad[:, :, R:2 * R]
+            return None, None
+        return finish_local
     up, down = (rank - 1) % world, (rank + 1) % world
-    first = x_pad[:, :, R:2 * R].contiguous()      # this band's first R rows
-    last = x_pad[:, :, Hb:Hb + R].contiguous()     # this band's last R rows
-    from_up = torch.empty_like(last)
-    from_down = torch.empty_like(first)
-    from_above = torch.empty_like(bot) if rank > 0 else None
-    from_below = torch.empty_like(top) if rank + 1 < world else None
+    from_up = from_down = from_above = from_below = None
+    sends, recvs = [], []
     # Messages between a pair match in issue order (with two ranks `up` and
     # `down` are the same peer): every rank sends last rows, first rows, top
     # strip, bottom strip, and receives in the matching order.
-    ops = [dist.P2POp(dist.isend, last, _g(down, group), group),
-           dist.P2POp(dist.isend, first, _g(up, group), group)]
-    if rank > 0:
-        ops.append(dist.P2POp(dist.isend, top.contiguous(), _g(up, group), group))
-    if rank + 1 < world:
-        ops.append(dist.P2POp(dist.isend, bot.contiguous(), _g(down, group), group))
-    ops += [dist.P2POp(dist.irecv, from_up, _g(up, group), group),
-            dist.P2POp(dist.irecv, from_down, _g(down, group), group)]
-    if from_above is not None:
-        ops.append(dist.P2POp(dist.irecv, from_above, _g(up, group), group))
-    if from_below is not None:
-        ops.append(dist.P2POp(dist.irecv, from_below, _g(down, group), group))
-    for req in dist.batch_isend_irecv(ops):
-        req.wait()
-    x_pad[:, :, :R] = from_up
-    x_pad[:, :, R + Hb:] = from_down
-    return from_below, from_above
+    if halo:
+        first = x_pad[:, :, R:2 * R].contiguous()      # this band's first R rows
+        last = x_pad[:, :, Hb:Hb + R].contiguous()     # this band's last R rows
+        from_up = torch.empty_like(last)
+        from_down = torch.empty_like(first)
+        sends += [(last, down), (first, up)]
+        recvs += [(from_up, up), (from_down, down)]
+    if strips:
+        from_above = torch.empty_like(bot) if rank > 0 else None
+        from_below = torch.empty_like(top) if rank + 1 < world else None
+        if rank > 0:
+            sends.append((top.contiguous(), up))
+        if rank + 1 < world:
+            sends.append((bot.contiguous(), down))
+        if from_above is not None:
+            recvs.append((from_above, up))
+        if from_below is not None:
+            recvs.append((from_below, down))
+    ops = ([dist.P2POp(dist.isend, t, _g(r, group), group) for t, r in sends]
+           + [dist.P2POp(dist.irecv, t, _g(r, group), group) for t, r in recvs])
+    reqs = dist.batch_isend_irecv(ops) if ops else []
+
+    def finish():
+        for req in reqs:
+            req.wait()
+        if halo:
+            x_pad[:, :, :R] = from_up
+            x_pad[:, :, R + Hb:] = from_down
+        return from_below, from_above
+    return finish
+
+
+def _reserve_sms() -> int:
+    import os
+    return int(os.environ.get("NSC_BAND_RESERVE_SMS", "2"))
 
 
 def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
                          compute: Optional[Callable] = None, *, padded: bool = False,
                          forward: Callable = band_forward_cuda,
-                         edges: Callable = band_edges_cuda):
+                         edges: Callable = band_edges_cuda,
+                         overlap: bool = True):
     """accumulate_uz of this rank's band of a row-split image.
 
     x_band: (B, C, Hb, W) this rank's rows of x -- or, with padded=True,
@@ -226,7 +267,10 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
     image.  Bands follow `band_rows(Hg, world, rank)` and must be at least R
     rows tall.  Returns this band's (U, Z) rows.  `compute`, when given,
     replaces both `forward` and `edges` with one call returning
-    (U, Z, top, bot) (run after the halo arrives)."""
+    (U, Z, top, bot) (run after the halo arrives).  overlap=True (CUDA
+    forward only): the x halo travels during the edge-strip kernel and the
+    strips during the band forward, which runs on all but
+    NSC_BAND_RESERVE_SMS (default 2) SMs."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -247,9 +291,30 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
             return compute(xe, wb, sh, r0, hg)[2:]
         def forward(xe, wb, sh, r0, hg):        # noqa: F811
             return compute(xe, wb, sh, r0, hg)[:2]
-    top, bot = edges(x_pad, w_band, shifts, row0, Hg)
-    from_below, from_above = exchange_halo_and_strips(x_pad, R, top, bot, group)
-    U, Z = forward(x_pad, w_band, shifts, row0, Hg)
+    import os
+    overlap = overlap and os.environ.get("NSC_BAND_OVERLAP", "1") != "0"
+    if (overlap and compute is None and forward is band_forward_cuda
+            and x_pad.is_cuda):
+        # x halo in flight during the edge-strip kernel; the strips in flight
+        # during the band forward, which leaves NSC_BAND_RESERVE_SMS SMs to
+        # the collective's kernels
+        finish_halo = exchange_start(x_pad, R, None, None, group, strips=False)
+        top, bot = edges(x_pad, w_band, shifts, row0, Hg)
+        finish_strips = exchange_start(x_pad, R, top, bot, group, halo=False)
+        finish_halo()
+        acc = (torch.float64 if torch.float64 in (x_pad.dtype, w_band.dtype)
+               else torch.float32)
+        U = torch.empty((x_pad.shape[0], x_pad.shape[1], Hb, x_pad.shape[3]),
+                        dtype=acc, device=x_pad.device)
+        Z = torch.empty_like(U)
+        nsm = torch.cuda.get_device_properties(x_pad.device).multi_processor_count
+        cap = max(1, nsm - _reserve_sms()) if world > 1 else 0
+        band_rows_cuda(x_pad, w_band, shifts, row0, Hg, 0, Hb, U, Z, cap)
+        from_below, from_above = finish_strips()
+    else:
+        top, bot = edges(x_pad, w_band, shifts, row0, Hg)
+        from_below, from_above = exchange_start(x_pad, R, top, bot, group)()
+        U, Z = forward(x_pad, w_band, shifts, row0, Hg)
     if R == 0 or world == 1:
         return U, Z
     return _add_strips(U, Z, from_below, from_above)

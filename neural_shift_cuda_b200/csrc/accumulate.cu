@@ -47,11 +47,11 @@ acc_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
                typename Acc<TX>::type* __restrict__ U,
                typename Acc<TX>::type* __restrict__ Z, const ShiftTable st,
                int64_t B, int64_t C, int64_t Hout, int64_t W, int64_t Cw,
-               XRows xr, int64_t groups) {
+               XRows xr, int64_t groups, int64_t hb0, int64_t hb1) {
     using A = typename Acc<TX>::type;
     const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
-    const int64_t h = static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
-    if (wcol >= W || h >= Hout) return;
+    const int64_t h = hb0 + static_cast<int64_t>(blockIdx.y) * kBY + threadIdx.y;
+    if (wcol >= W || h >= hb1) return;
     const int64_t plane_x = xr.H * W;
     const int64_t plane_o = Hout * W;
     const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
@@ -380,7 +380,8 @@ nsc_status acc_fwd_generic(const void* x, int xd, const void* w, int wd,
                            int64_t Cw, int64_t B, int64_t C, int64_t Hout,
                            int64_t W, int64_t x_rows, int64_t x_off, int wrap,
                            const ShiftTable& st, void* U, void* Z,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int64_t h_begin, int64_t h_end) {
+    if (h_end < 0) h_end = Hout;
     XRows xr{x_rows, x_off, wrap};
     return with_types("accumulate_uz", xd, wd, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
@@ -389,11 +390,12 @@ nsc_status acc_fwd_generic(const void* x, int xd, const void* w, int wd,
         with_nc(C, Cw, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             const int64_t groups = n_groups(B, C, Cw, NC);
-            acc_fwd_kernel<TX, TW, NC><<<grid_for(W, Hout, groups),
+            if (h_end <= h_begin) return;
+            acc_fwd_kernel<TX, TW, NC><<<grid_for(W, h_end - h_begin, groups),
                                           dim3(kBX, kBY), 0, stream>>>(
                 static_cast<const TX*>(x), static_cast<const TW*>(w),
                 static_cast<A*>(U), static_cast<A*>(Z), st, B, C, Hout, W, Cw,
-                xr, groups);
+                xr, groups, h_begin, h_end);
         });
         return check_launch("accumulate_uz");
     });
@@ -575,6 +577,38 @@ nsc_status nsc_accumulate_uz_band_fwd(const void* x_ext, int x_dtype,
         return check_launch("accumulate_uz_band");
     return acc_fwd_generic(x_ext, x_dtype, w, w_dtype, w_channels, B, C, Hb, W,
                            Hb + 2 * R, R, 0, st, U, Z, as_stream(stream));
+}
+
+nsc_status nsc_accumulate_uz_band_rows_fwd(const void* x_ext, int x_dtype,
+                                           const void* w, int w_dtype,
+                                           int64_t w_channels, int64_t B, int64_t C,
+                                           int64_t Hb, int64_t W, int64_t row0,
+                                           int64_t Hg, int64_t r_begin, int64_t r_end,
+                                           int max_ctas, const int64_t* shifts,
+                                           int64_t S, void* U, void* Z,
+                                           void* stream) {
+    using namespace nsc;
+    const char* op = "accumulate_uz_band_rows";
+    ShiftTable st;
+    nsc_status e = check_common(op, x_dtype, w_dtype, w_channels, B, C, Hg, W,
+                                shifts, S, &st);
+    if (e) return e;
+    e = band_checks(op, Hb, row0, Hg, st);
+    if (e) return e;
+    if (r_begin < 0 || r_begin > r_end || r_end > Hb)
+        return fail(NSC_ERR_INVALID_ARG, "%s: rows [%lld, %lld) outside the band of %lld",
+                    op, (long long)r_begin, (long long)r_end, (long long)Hb);
+    if (max_ctas < 0) return fail(NSC_ERR_INVALID_ARG, "%s: max_ctas < 0", op);
+    if (B == 0 || C == 0 || W == 0 || r_begin == r_end) return ok();
+    if (!x_ext || !w || !U || !Z)
+        return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
+    const int64_t R = st.R;
+    if (acc_fwd_fast(x_ext, x_dtype, w, w_dtype, w_channels, B, C, Hb, W,
+                     Hb + 2 * R, R, 0, st, U, Z, as_stream(stream), 0, nullptr,
+                     r_begin, r_end, max_ctas))
+        return check_launch(op);
+    return acc_fwd_generic(x_ext, x_dtype, w, w_dtype, w_channels, B, C, Hb, W,
+                           Hb + 2 * R, R, 0, st, U, Z, as_stream(stream), r_begin, r_end);
 }
 
 nsc_status nsc_accumulate_uz_band_edges(const void* x_ext, int x_dtype,

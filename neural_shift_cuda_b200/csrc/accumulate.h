@@ -12,18 +12,22 @@ nsc_status acc_fwd_generic(const void* x, int xd, const void* w, int wd,
                            int64_t Cw, int64_t B, int64_t C, int64_t Hout,
                            int64_t W, int64_t x_rows, int64_t x_off, int wrap,
                            const ShiftTable& st, void* U, void* Z,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int64_t h_begin = 0,
+                           int64_t h_end = -1);
 
 // Tiled fast forward.  Returns false (launching nothing) when the geometry
 // or dtypes are outside what it handles; the caller then uses the generic
 // path.  mode 0: accumulate_uz (U, Z); mode 1 / 2: normalized_accumulate_uz
 // with log / positive weights (U <- D, Z <- log_C, `invalid` flag word),
-// full images only (wrap != 0).
+// full images only (wrap != 0).  Only output rows [h_begin, h_end) are
+// computed (h_end < 0: all); max_ctas > 0 caps the persistent grid (CTAs
+// left free for a concurrent collective).
 bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                   int64_t B, int64_t C, int64_t Hout, int64_t W,
                   int64_t x_rows, int64_t x_off, int wrap,
                   const ShiftTable& st, void* U, void* Z, cudaStream_t stream,
-                  int mode = 0, int* invalid = nullptr);
+                  int mode = 0, int* invalid = nullptr, int64_t h_begin = 0,
+                  int64_t h_end = -1, int max_ctas = 0);
 
 // Why the last acc_fwd_fast call on this thread declined ("" if it ran).
 const char* fast_decline_reason();

@@ -84,9 +84,12 @@ bool by_bucket(int mode, bool exact, int K, const fast::WMaps& maps,
 bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                   int64_t B, int64_t C, int64_t Hout, int64_t W, int64_t x_rows,
                   int64_t x_off, int wrap, const ShiftTable& st, void* U, void* Z,
-                  cudaStream_t stream, int mode, int* invalid) {
+                  cudaStream_t stream, int mode, int* invalid, int64_t h_begin,
+                  int64_t h_end, int max_ctas) {
     using namespace fast;
     g_decline = "";
+    if (h_end < 0) h_end = Hout;
+    if (h_begin < 0 || h_begin > h_end || h_end > Hout) DECLINE("row range");
     if (mode != 0 && !wrap) DECLINE("normalized modes take full images only");
     if (std::getenv("NSC_DISABLE_FAST")) DECLINE("disabled by NSC_DISABLE_FAST");
     if (st.any_per) DECLINE("periodic mirror rows");
@@ -218,7 +221,10 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     g.x_rows = x_rows; g.x_off = x_off; g.wrap = wrap;
     const int TW = TPR * V;
     g.tiles_x = static_cast<int32_t>((W + TW - 1) / TW);
-    g.tiles_y = static_cast<int32_t>((Hout + TH - 1) / TH);
+    g.hb0 = static_cast<int32_t>(h_begin);
+    g.hb1 = static_cast<int32_t>(h_end);
+    g.max_ctas = max_ctas;
+    g.tiles_y = static_cast<int32_t>((h_end - h_begin + TH - 1) / TH);
     g.groups = B * (Cw == 1 ? 1 : C);
     g.ntiles = g.groups * g.tiles_y * g.tiles_x;
     const int XC = align_up(K, V);

@@ -113,6 +113,8 @@ struct Geo {
     int32_t XH, XW;             // x halo tile
     int32_t col_border;         // W is not a multiple of the tile width
     int32_t nstage;             // weight ring depth
+    int32_t hb0, hb1;           // output rows computed: [hb0, hb1) of [0, H)
+    int32_t max_ctas;           // grid cap (0: one CTA per SM)
     uint32_t plane_bytes;       // one plane of a weight box in shared memory
 };
 
@@ -141,7 +143,7 @@ __device__ __forceinline__ TileId decode_tile(int64_t tile, const Geo& g, int TW
     TileId id;
     id.grp = grp;
     id.b = grp / cgroups;
-    id.h0 = static_cast<int>(ty) * TH;
+    id.h0 = g.hb0 + static_cast<int>(ty) * TH;
     id.w0 = static_cast<int>(tx) * TW;
     return id;
 }
@@ -800,9 +802,9 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                     for (int c = 0; c < NC; ++c) u[c][i] = u[c][i] / sv;
                 }
             }
-            if (bad && invalid && h < g.H && wcol < g.W) atomicOr(invalid, 1);
+            if (bad && invalid && h < g.hb1 && wcol < g.W) atomicOr(invalid, 1);
         }
-        if (h < g.H && wcol < g.W) {
+        if (h < g.hb1 && wcol < g.W) {
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const int64_t o = ((b * g.C + c0 + c) * g.H + h) * g.W + wcol;

@@ -56,7 +56,9 @@ bool launch(const WMaps& maps, const void* x, void* U, void* Z,
         return false;
     }
     const int64_t nsm = fast_sm_count();
-    const unsigned grid = static_cast<unsigned>(g.ntiles < nsm ? g.ntiles : nsm);
+    int64_t grid_cap = nsm;
+    if (g.max_ctas > 0 && g.max_ctas < grid_cap) grid_cap = g.max_ctas;
+    const unsigned grid = static_cast<unsigned>(g.ntiles < grid_cap ? g.ntiles : grid_cap);
     k<<<grid, NTHREADS, smem, stream>>>(maps, static_cast<const T*>(x),
                                         static_cast<float*>(U),
                                         static_cast<float*>(Z), tab, g, timeouts, ticket,

@@ -149,8 +149,9 @@ def test_fullsize_config5_properties(cuda):
     assert _lib.wait_timeouts() == 0
 
 
+@pytest.mark.parametrize("overlap", [False, True])
 @pytest.mark.parametrize("padded", [False, True])
-def test_banded_single_rank_process_group(cuda, padded):
+def test_banded_single_rank_process_group(cuda, padded, overlap):
     """accumulate_uz_banded through a one-rank process group: the halo is
     the band's own circular wrap and no strips travel; the result equals
     the unsplit op (plain and padded x buffers)."""
@@ -173,8 +174,32 @@ def test_banded_single_rank_process_group(cuda, padded):
             xp = torch.full((1, 3, 40 + 2 * R, 64), float("nan"), dtype=x.dtype, device=cuda)
             xp[:, :, R:R + 40] = xb
             xb = xp
-        U, Z = bands.accumulate_uz_banded(xb, w.to(cuda), sh, 40, padded=padded)
+        U, Z = bands.accumulate_uz_banded(xb, w.to(cuda), sh, 40, padded=padded,
+                                          overlap=overlap)
         torch.testing.assert_close(U, U0, rtol=1e-6, atol=1e-5)
         torch.testing.assert_close(Z, Z0, rtol=1e-6, atol=1e-5)
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dtype,R,Hb", [(torch.float16, 10, 100), (torch.float32, 3, 37),
+                                       (torch.bfloat16, 5, 10)])
+def test_band_rows_pieces_equal_band_forward(cuda, dtype, R, Hb):
+    """nsc_accumulate_uz_band_rows_fwd: interior rows with a capped grid plus
+    the two border pieces reproduce the whole band forward exactly."""
+    from neural_shift_cuda_b200 import bands
+    torch.manual_seed(9)
+    sh = T(O.halfplane_shifts(R))
+    S = len(sh)
+    Hg, W, row0 = 4 * Hb, 128, Hb
+    x = torch.rand(1, 3, Hg, W).to(dtype).to(cuda)
+    w = torch.rand(S, 1, Hg, W).to(dtype).to(cuda)
+    xe = bands.x_ext_from_full(x, row0, Hb, R)
+    wb = w[:, :, row0:row0 + Hb].contiguous()
+    U0, Z0 = bands.band_forward_cuda(xe, wb, sh, row0, Hg)
+    U = torch.full_like(U0, float("nan"))
+    Z = torch.full_like(Z0, float("nan"))
+    bands.band_rows_cuda(xe, wb, sh, row0, Hg, R, Hb - R, U, Z, max_ctas=100)
+    bands.band_rows_cuda(xe, wb, sh, row0, Hg, 0, R, U, Z)
+    bands.band_rows_cuda(xe, wb, sh, row0, Hg, Hb - R, Hb, U, Z)
+    assert torch.equal(U, U0) and torch.equal(Z, Z0)
