@@ -79,6 +79,22 @@ NSC_API const char* nsc_last_error_string(void);
  * returns 0xFFFFFFFF if the counter cannot be read. */
 NSC_API unsigned int nsc_wait_timeouts(void);
 
+/* Synchronizes `stream` and returns NSC_ERR_TIMEOUT when bounded device
+ * waits of the current device gave up since the previous nsc_check_waits
+ * on that device (the kernels concerned returned early; their outputs are
+ * undefined), NSC_OK otherwise.  No counterpart in the reference (whose
+ * kernels have no waits); the host-side status of the bounded-wait design. */
+NSC_API nsc_status nsc_check_waits(void* stream);
+
+/* Test hook, no counterpart in the reference: subsequent tiled
+ * accumulate / normalized launches leave weight copy number `skip_copy`
+ * (per CTA, counted from 0; -1 = none) unissued and give every bounded
+ * wait `wait_budget` hinted sleeps of about 1 ms (0 = the default of
+ * 4096).  With a skipped copy the consumers' waits on it run out, the
+ * kernel returns early and nsc_check_waits reports NSC_ERR_TIMEOUT; the
+ * context stays usable.  Reset with nsc_test_wait_fault(-1, 0). */
+NSC_API void nsc_test_wait_fault(int skip_copy, unsigned int wait_budget);
+
 /* ---------------------------------------------------------------------
  * Gathers.  Replace shift_gather_forward / pair_gather_forward
  * (csrc/shift_ops.cpp:81-140) and their backward (shift_ops.cpp:102-156).

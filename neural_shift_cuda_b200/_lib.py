@@ -68,13 +68,14 @@ _SIGS = {
                                    _L, _I, _D, _P, _P, _P],
     "nsc_metropolis_bwd": [_P, _I, _L, _P, _I, _L, _L, _L, _L, _LP, _L, _I,
                            _D, _P, _P, _P, _P, _P, _P, _P, _P],
+    "nsc_check_waits": [_P],
     "nsc_nectr_fused_fwd": [_P, _P, _I, _L, _L, _L, _L, _L, _I,
                             ctypes.POINTER(ctypes.c_double), _L, _D, _D, _D, _D,
                             _LP, _L, _I, _P, _P, _P, _P],
 }
 
 EXPORTED = ["nsc_index_width_bits", "nsc_version", "nsc_last_error_string",
-            "nsc_wait_timeouts", *_SIGS]
+            "nsc_wait_timeouts", "nsc_test_wait_fault", *_SIGS]
 
 
 def load() -> ctypes.CDLL:
@@ -91,6 +92,8 @@ def load() -> ctypes.CDLL:
             lib.nsc_version.restype = ctypes.c_char_p
             lib.nsc_last_error_string.restype = ctypes.c_char_p
             lib.nsc_wait_timeouts.restype = ctypes.c_uint
+            lib.nsc_test_wait_fault.argtypes = [ctypes.c_int, ctypes.c_uint]
+            lib.nsc_test_wait_fault.restype = None
             for name, args in _SIGS.items():
                 fn = getattr(lib, name)
                 fn.argtypes = args
@@ -120,6 +123,22 @@ def index_width_bits() -> int:
 def wait_timeouts() -> int:
     """Bounded device waits that gave up on the current device (synchronizes)."""
     return int(load().nsc_wait_timeouts())
+
+
+def check_device_waits(device=None) -> None:
+    """Synchronize the current stream of `device` and raise RuntimeError
+    ([NSC_ERR_TIMEOUT]) if a bounded device wait gave up since the previous
+    check: a tiled kernel then returned early with undefined outputs."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    with torch.cuda.device(dev):
+        call("nsc_check_waits", ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+
+
+def test_wait_fault(skip_copy: int = -1, wait_budget: int = 0) -> None:
+    """Test hook (nsc_test_wait_fault): leave copy `skip_copy` of every CTA
+    of later tiled launches unissued, with `wait_budget` ~1 ms sleeps per
+    bounded wait; (-1, 0) restores normal operation."""
+    load().nsc_test_wait_fault(int(skip_copy), int(wait_budget))
 
 
 def version() -> str:

@@ -193,12 +193,20 @@ def exchange_halo_and_strips(x_pad: torch.Tensor, R: int, top, bot, group=None):
     return exchange_start(x_pad, R, top, bot, group)()
 
 
+class BandExchangeError(RuntimeError):
+    """A neighbour rank did not complete the band exchange (it left, or
+    missed the deadline)."""
+
+
 def exchange_start(x_pad: torch.Tensor, R: int, top, bot, group=None,
-                   halo: bool = True, strips: bool = True):
+                   halo: bool = True, strips: bool = True,
+                   deadline: Optional[float] = None):
     """Issue the grouped send/recv of `exchange_halo_and_strips` -- the x
     halo, the mirror strips or both -- and return a `finish()` that waits
     for it (the current stream waits on the collective), writes the halo
-    rows into x_pad and returns (from_below, from_above)."""
+    rows into x_pad and returns (from_below, from_above).  With `deadline`
+    (seconds) a send/recv that has not completed in time -- or fails
+    because the peer left -- raises BandExchangeError on the host."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -240,7 +248,20 @@ def exchange_start(x_pad: torch.Tensor, R: int, top, bot, group=None,
 
     def finish():
         for req in reqs:
-            req.wait()
+            if deadline is None:
+                req.wait()
+                continue
+            from datetime import timedelta
+            try:
+                done = req.wait(timeout=timedelta(seconds=deadline))
+            except RuntimeError as e:
+                raise BandExchangeError(
+                    f"rank {rank}: band exchange with ranks {up} / {down} failed "
+                    f"within {deadline} s: {e}") from e
+            if done is False:
+                raise BandExchangeError(
+                    f"rank {rank}: band exchange with ranks {up} / {down} did not "
+                    f"complete within {deadline} s")
         if halo:
             x_pad[:, :, :R] = from_up
             x_pad[:, :, R + Hb:] = from_down
@@ -257,7 +278,7 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
                          compute: Optional[Callable] = None, *, padded: bool = False,
                          forward: Callable = band_forward_cuda,
                          edges: Callable = band_edges_cuda,
-                         overlap: bool = True):
+                         overlap: bool = True, deadline: Optional[float] = None):
     """accumulate_uz of this rank's band of a row-split image.
 
     x_band: (B, C, Hb, W) this rank's rows of x -- or, with padded=True,
@@ -270,7 +291,9 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
     (U, Z, top, bot) (run after the halo arrives).  overlap=True (CUDA
     forward only): the x halo travels during the edge-strip kernel and the
     strips during the band forward, which runs on all but
-    NSC_BAND_RESERVE_SMS (default 2) SMs."""
+    NSC_BAND_RESERVE_SMS (default 2) SMs.  deadline (seconds): an exchange
+    that has not completed in time, or whose peer left, raises
+    BandExchangeError (the process group's own timeout applies otherwise)."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -298,9 +321,11 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
         # x halo in flight during the edge-strip kernel; the strips in flight
         # during the band forward, which leaves NSC_BAND_RESERVE_SMS SMs to
         # the collective's kernels
-        finish_halo = exchange_start(x_pad, R, None, None, group, strips=False)
+        finish_halo = exchange_start(x_pad, R, None, None, group, strips=False,
+                                     deadline=deadline)
         top, bot = edges(x_pad, w_band, shifts, row0, Hg)
-        finish_strips = exchange_start(x_pad, R, top, bot, group, halo=False)
+        finish_strips = exchange_start(x_pad, R, top, bot, group, halo=False,
+                                       deadline=deadline)
         finish_halo()
         acc = (torch.float64 if torch.float64 in (x_pad.dtype, w_band.dtype)
                else torch.float32)
@@ -313,7 +338,8 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
         from_below, from_above = finish_strips()
     else:
         top, bot = edges(x_pad, w_band, shifts, row0, Hg)
-        from_below, from_above = exchange_start(x_pad, R, top, bot, group)()
+        from_below, from_above = exchange_start(x_pad, R, top, bot, group,
+                                                deadline=deadline)()
         U, Z = forward(x_pad, w_band, shifts, row0, Hg)
     if R == 0 or world == 1:
         return U, Z

@@ -219,6 +219,13 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     Geo g{};
     g.B = B; g.C = C; g.H = Hout; g.W = W; g.Cw = Cw;
     g.x_rows = x_rows; g.x_off = x_off; g.wrap = wrap;
+    {
+        int skip;
+        unsigned budget;
+        wait_fault_settings(&skip, &budget);
+        g.skip_copy = skip;
+        g.wait_budget = budget;
+    }
     const int TW = TPR * V;
     g.tiles_x = static_cast<int32_t>((W + TW - 1) / TW);
     g.hb0 = static_cast<int32_t>(h_begin);

@@ -115,6 +115,8 @@ struct Geo {
     int32_t nstage;             // weight ring depth
     int32_t hb0, hb1;           // output rows computed: [hb0, hb1) of [0, H)
     int32_t max_ctas;           // grid cap (0: one CTA per SM)
+    uint32_t wait_budget;       // hinted sleeps (~1 ms each) before a wait gives up
+    int32_t skip_copy;          // test hook: this copy index is never issued (-1: none)
     uint32_t plane_bytes;       // one plane of a weight box in shared memory
 };
 
@@ -518,11 +520,18 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                     const int len = (e >> kLenShift) & 7;
                     if (e < 0 || len == 0) continue;
                     const int s = e & kSMask;
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, timeouts) ||
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, timeouts, g.wait_budget) ||
                         *(volatile int*)&abort_flag) {
                         aborted = true;
                         *(volatile int*)&abort_flag = 1;
                         break;
+                    }
+                    if (static_cast<int32_t>(it) == g.skip_copy) {
+                        // test hook: leave this stage's copy unissued, so the
+                        // consumers' bounded waits on it give up
+                        ++it;
+                        if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+                        continue;
                     }
                     mbar_arrive_expect_tx(&full[stage], len * g.plane_bytes);
                     const int mo = dy > 0 ? align_up(dy, V) : 0;
@@ -543,7 +552,8 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         // flight.  Wait (bounded) for the last NSTAGE loads to land.
         const uint32_t n = it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE;
         for (uint32_t j = it - n; j < it; ++j)
-            mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts);
+            if (static_cast<int32_t>(j) != g.skip_copy)
+                mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts, g.wait_budget);
         return;
     }
 
@@ -597,7 +607,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
 
     // Tile k of this CTA (ring slot k & 3), -1 when the schedule is done.
     auto tile_at = [&](uint32_t k) -> int64_t {
-        if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts)) {
+        if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts, g.wait_budget)) {
             dead = true;
             *(volatile int*)&abort_flag = 1;
         }
@@ -700,7 +710,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 constexpr int dy = decltype(dyc)::value;
                 if (pos == 0)
                     mbar_wait32_ab(full32 + 8 * stage, phase, timeouts,
-                                   (volatile int*)&abort_flag);
+                                   (volatile int*)&abort_flag, g.wait_budget);
                 const uint32_t sp = after(stp) + pos * g.plane_bytes;
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];

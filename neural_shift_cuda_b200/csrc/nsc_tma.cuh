@@ -94,9 +94,10 @@ __device__ __forceinline__ void mbar_arrive32(uint32_t bar) {
 // timeout) when the budget runs out.
 constexpr uint32_t kSleepWaits = 4096;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          unsigned int* timeouts) {
+                                          unsigned int* timeouts,
+                                          uint32_t budget = kSleepWaits) {
     if (mbar_try_wait(bar, parity)) return true;
-    for (uint32_t i = 0; i < kSleepWaits; ++i)
+    for (uint32_t i = 0; i < budget; ++i)
         if (mbar_try_wait_sleep(bar, parity)) return true;
     atomicAdd(timeouts, 1u);
     return false;
@@ -107,9 +108,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // complete) is a single try_wait.
 static __device__ __noinline__ bool mbar_wait32_slow(uint32_t bar, uint32_t parity,
                                               unsigned int* timeouts,
-                                              volatile int* abort_flag) {
+                                              volatile int* abort_flag,
+                                              uint32_t budget) {
     if (*abort_flag) return false;
-    for (uint32_t i = 0; i < kSleepWaits; ++i) {
+    for (uint32_t i = 0; i < budget; ++i) {
         if (mbar_try_wait_sleep32(bar, parity)) return true;
         if ((i & 63u) == 63u && *abort_flag) return false;
     }
@@ -119,9 +121,10 @@ static __device__ __noinline__ bool mbar_wait32_slow(uint32_t bar, uint32_t pari
 }
 __device__ __forceinline__ bool mbar_wait32_ab(uint32_t bar, uint32_t parity,
                                                unsigned int* timeouts,
-                                               volatile int* abort_flag) {
+                                               volatile int* abort_flag,
+                                               uint32_t budget = kSleepWaits) {
     if (mbar_try_wait32(bar, parity)) return true;
-    return mbar_wait32_slow(bar, parity, timeouts, abort_flag);
+    return mbar_wait32_slow(bar, parity, timeouts, abort_flag, budget);
 }
 __device__ __forceinline__ bool mbar_wait32(uint32_t bar, uint32_t parity,
                                             unsigned int* timeouts) {
@@ -164,6 +167,10 @@ __device__ __forceinline__ void named_sync(int id, int count) {
 // Host: device address of the wait-timeout counter of the current device
 // (nullptr on failure, with the error recorded).
 unsigned int* wait_timeout_counter();
+
+// Host: the wait budget (hinted sleeps) and the test hook's skipped copy
+// index (-1: none) the next tiled launch uses (set by nsc_test_wait_fault).
+void wait_fault_settings(int* skip_copy, unsigned* budget);
 
 // Host: encode a 3-D tensor map {W, H, planes} with box {bw, bh, 1}.
 // Returns false with a message in `err` when the driver refuses.

@@ -2,6 +2,7 @@
 // through the driver entry point (no link-time dependency on libcuda) and
 // the per-device wait-timeout counter.
 #include <cudaTypedefs.h>
+#include <atomic>
 #include <mutex>
 
 #include "nsc_host.h"
@@ -104,6 +105,47 @@ bool encode_map_3d(CUtensorMap* map, const void* base, int elem_bytes,
 }
 
 }  // namespace nsc
+
+namespace nsc {
+namespace {
+unsigned int g_seen[kMaxDev] = {};
+std::atomic<int> g_test_skip{-1};
+std::atomic<unsigned> g_test_budget{0};
+}  // namespace
+
+void wait_fault_settings(int* skip_copy, unsigned* budget) {
+    *skip_copy = g_test_skip.load();
+    const unsigned b = g_test_budget.load();
+    *budget = b ? b : kSleepWaits;
+}
+}  // namespace nsc
+
+extern "C" NSC_API nsc_status nsc_check_waits(void* stream) {
+    using namespace nsc;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev)
+        return fail(NSC_ERR_LAUNCH_FAILED, "check_waits: no current device");
+    cudaError_t e = cudaStreamSynchronize(as_stream(stream));
+    if (e != cudaSuccess)
+        return fail(NSC_ERR_LAUNCH_FAILED, "check_waits: %s", cudaGetErrorString(e));
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess)
+        return fail(NSC_ERR_LAUNCH_FAILED, "check_waits: cannot read the wait counter");
+    std::lock_guard<std::mutex> lock(g_mu);
+    const unsigned int before = g_seen[dev];
+    g_seen[dev] = v;
+    if (v != before)
+        return fail(NSC_ERR_TIMEOUT,
+                    "%u bounded device wait(s) gave up since the last check: a "
+                    "tiled kernel returned early and its outputs are undefined",
+                    v - before);
+    return ok();
+}
+
+extern "C" NSC_API void nsc_test_wait_fault(int skip_copy, unsigned int wait_budget) {
+    nsc::g_test_skip.store(skip_copy);
+    nsc::g_test_budget.store(wait_budget);
+}
 
 extern "C" NSC_API unsigned int nsc_wait_timeouts(void) {
     unsigned int v = 0;

@@ -115,3 +115,45 @@ def test_band_rows_cover_image():
         for (a, n), (b, _) in zip(spans, spans[1:]):
             assert a + n == b
         assert spans[-1][0] + spans[-1][1] == Hg
+
+
+def _leaver_worker(rank, world, port, out):
+    """Step 1 on every rank; then rank world-1 leaves (exits without
+    shutting its process group down) and the others run step 2, which must
+    fail on the host with BandExchangeError within the deadline."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=20))
+    Hg, W, R = 15, 6, 2
+    g = torch.Generator().manual_seed(0)
+    rows = O.halfplane_shifts(R)
+    sh = torch.tensor(rows)
+    x = torch.rand(1, 1, Hg, W, generator=g, dtype=torch.float64)
+    w = torch.rand(len(rows), 1, Hg, W, generator=g, dtype=torch.float64)
+    row0, Hb = bands.band_rows(Hg, world, rank)
+    args = (x[:, :, row0:row0 + Hb].contiguous(), w[:, :, row0:row0 + Hb].contiguous(),
+            sh, Hg)
+    bands.accumulate_uz_banded(*args, compute=_band_compute_cpu, deadline=5.0)
+    dist.barrier()
+    if rank == world - 1:
+        out[rank] = 1
+        os._exit(0)                      # leaves between steps
+    t0 = time.monotonic()
+    try:
+        bands.accumulate_uz_banded(*args, compute=_band_compute_cpu, deadline=5.0)
+        out[rank] = 0                    # should not complete
+    except bands.BandExchangeError:
+        out[rank] = 1 if time.monotonic() - t0 < 15.0 else 2
+    os._exit(0)
+
+
+def test_banded_rank_leaves_between_steps():
+    world = 3
+    ctx = mp.get_context("spawn")
+    out = ctx.Array("i", [0] * world)
+    mp.start_processes(_leaver_worker, args=(world, _free_port(), out),
+                       nprocs=world, join=True, start_method="spawn")
+    assert list(out) == [1] * world
