@@ -70,3 +70,31 @@ def test_noalloc_rejects_oversized_problem(cuda):
     x = torch.zeros(17, 1, 512, 512, device=cuda)
     with pytest.raises(RuntimeError, match="built-in scratch"):
         _run("nsc_metropolis_fwd_noalloc", w, x, [(0, 0, 0)], True, 1e-6)
+
+
+def test_noalloc_fp64_at_the_limit_and_one_pixel_kernels(cuda, monkeypatch):
+    """fp64 degree values are 8 bytes: B * Cw * H * W = 2^21 fills the
+    16 MiB array exactly and one more column is rejected.  With
+    NSC_METRO_GENERIC=1 the one-pixel degree and aggregation kernels run
+    instead of the tiled ones; both forms must overwrite every scratch value
+    they read (two calls in a row, the second smaller)."""
+    w, x, rows = _case(5, 2, 3, 1, 1024, 1024, 2, cuda)
+    w, x = w.double(), x.double()
+    degree = torch.empty((2, 1, 1024, 1024), dtype=torch.float64, device=cuda)
+    Wx_a, dh_a = _run("nsc_metropolis_fwd", w, x, rows, True, 1e-6, degree)
+    Wx_n, dh_n = _run("nsc_metropolis_fwd_noalloc", w, x, rows, True, 1e-6)
+    torch.testing.assert_close(Wx_n, Wx_a, rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(dh_n, dh_a, rtol=1e-12, atol=1e-12)
+    wbig = torch.zeros(2, 1, 1, 1024, 1025, dtype=torch.float64, device=cuda)
+    xbig = torch.zeros(2, 1, 1024, 1025, dtype=torch.float64, device=cuda)
+    with pytest.raises(RuntimeError, match="built-in scratch"):
+        _run("nsc_metropolis_fwd_noalloc", wbig, xbig, [(0, 0, 0)], True, 1e-6)
+    monkeypatch.setenv("NSC_METRO_GENERIC", "1")
+    for seed, (B, C, Cw, H, W, R) in [(6, (2, 3, 1, 40, 48, 3)), (7, (1, 3, 3, 17, 23, 2))]:
+        w, x, rows = _case(seed, B, C, Cw, H, W, R, cuda)
+        degree = torch.empty((B, Cw, H, W), dtype=torch.float32, device=cuda)
+        Wx_a, dh_a = _run("nsc_metropolis_fwd", w, x, rows, True, 1e-6, degree)
+        Wx_n, dh_n = _run("nsc_metropolis_fwd_noalloc", w, x, rows, True, 1e-6)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(Wx_n, Wx_a, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(dh_n, dh_a, rtol=1e-5, atol=1e-5)
