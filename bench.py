@@ -655,7 +655,52 @@ def _wl_nectr(dtype_name, fused=True):
         f"{dtype_name} model, f32 accumulate", make, cpu)
 
 
-WORKLOADS = {"pair_gather": _wl_pair_gather, "normalized": _wl_normalized,
+def _wl_accumulate_train():
+    """configs[4] forward + backward: one training step of the reduction
+    (U, Z from x and the weights; grad_x, grad_w from grad_U, grad_Z)."""
+    Hs = Ws = 8192
+
+    def make(dev, b0, nb):
+        import neural_shift_cuda_b200 as nsc
+        x, w = make_band(0, Hs, dev)
+        gU = torch.randn((1, C, Hs, Ws), device=dev)
+        gZ = torch.randn((1, C, Hs, Ws), device=dev)
+        sh = torch.tensor(ROWS)
+
+        def run(xi, wi, a, b):
+            xi = xi.detach().requires_grad_(True)
+            wi = wi.detach().requires_grad_(True)
+            U, Z = nsc.accumulate_uz(xi, wi, sh)
+            gx, gw = torch.autograd.grad((U, Z), (xi, wi), (a, b))
+            return U.detach(), Z.detach(), gx, gw
+        return dict(inputs=[x, w, gU, gZ], run=run, launches=2,
+                    units=2 * S * C * Hs * Ws)
+
+    def cpu(nb):
+        from oracle import nsc_oracle as O
+        g = torch.Generator().manual_seed(0)
+        rows_s = 8
+        x = torch.rand(1, C, rows_s, Ws, generator=g).half()
+        w = torch.nn.functional.softplus(torch.randn(S, 1, rows_s, Ws, generator=g)).half()
+        gU = torch.randn(1, C, rows_s, Ws, generator=g)
+        gZ = torch.randn(1, C, rows_s, Ws, generator=g)
+        sh = torch.tensor(ROWS)
+        t0 = time.perf_counter()
+        O.accumulate_uz(x, w.expand(-1, C, -1, -1).contiguous(), sh)
+        O.accumulate_uz_backward(x, w, gU, gZ, sh)
+        return (2 * S * C * rows_s * Ws, time.perf_counter() - t0,
+                f"oracle accumulate_uz forward + backward on a (1, 3, {rows_s}, 8192) band, S=221")
+
+    return OpWorkload(
+        "accumulate_train", "pixel-shifts/s (accumulate_uz fwd+bwd, 8192^2 x3, S=221, "
+        "fp16 in / fp32 acc)", 1,
+        {"workload": "accumulate_uz forward + backward, configs[4] shapes (x fp16 "
+                     "(1,3,8192,8192), channel-shared fp16 weights (221,1,8192,8192), "
+                     "grad_U / grad_Z fp32 N(0,1))"},
+        "f16 in, f32 accumulate", make, cpu)
+
+
+WORKLOADS = {"pair_gather": _wl_pair_gather, "accumulate_train": _wl_accumulate_train, "normalized": _wl_normalized,
              "metropolis": _wl_metropolis,
              "nectr": lambda: _wl_nectr("f32"),
              "nectr_bf16": lambda: _wl_nectr("bf16"),

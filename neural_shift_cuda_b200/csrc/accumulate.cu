@@ -451,6 +451,9 @@ nsc_status acc_bwd(const void* x, int xd, const void* w, int wd, int64_t Cw,
                    int64_t B, int64_t C, int64_t H, int64_t W,
                    const ShiftTable& st, const void* gU, const void* gZ,
                    void* gx, void* gw, cudaStream_t stream) {
+    // grad_w by the tiled correlation kernel when it takes the call; the
+    // general kernel then computes grad_x only
+    const bool gw_done = acc_gw_fast(x, xd, wd, Cw, B, C, H, W, st, gU, gZ, gw, stream);
     return with_types("accumulate_uz_backward", xd, wd, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
@@ -458,7 +461,14 @@ nsc_status acc_bwd(const void* x, int xd, const void* w, int wd, int64_t Cw,
         with_nc(C, Cw, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             const int64_t groups = n_groups(B, C, Cw, NC);
-            if (Cw == 1 && C > NC) {
+            if (gw_done) {
+                acc_bwd_kernel<TX, TW, NC, false><<<grid_for(W, H, groups),
+                                                     dim3(kBX, kBY), 0, stream>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<const A*>(gU), static_cast<const A*>(gZ),
+                    static_cast<A*>(gx), static_cast<TW*>(gw), st, B, C, H, W, Cw,
+                    groups);
+            } else if (Cw == 1 && C > NC) {
                 acc_bwd_kernel<TX, TW, NC, false><<<grid_for(W, H, groups),
                                                      dim3(kBX, kBY), 0, stream>>>(
                     static_cast<const TX*>(x), static_cast<const TW*>(w),

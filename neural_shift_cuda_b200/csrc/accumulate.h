@@ -29,6 +29,12 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
                   int mode = 0, int* invalid = nullptr, int64_t h_begin = 0,
                   int64_t h_end = -1, int max_ctas = 0);
 
+// Tiled grad_w of accumulate_uz (x, w share fp16 / bf16 / fp32 storage,
+// grad_U / grad_Z fp32); false (nothing launched) when it declines.
+bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C,
+                 int64_t H, int64_t W, const ShiftTable& st, const void* gU,
+                 const void* gZ, void* gw, cudaStream_t stream);
+
 // Why the last acc_fwd_fast call on this thread declined ("" if it ran).
 const char* fast_decline_reason();
 

@@ -1,0 +1,58 @@
+"""GPU parity of the accumulate_uz backward with the tiled grad_w kernel
+(csrc/accumulate_gw.cu) against the oracle, and against the general
+kernel (NSC_DISABLE_FAST=1 declines every tiled path).  Tolerance: fp32
+rtol/atol 1e-4 on gradients of sums of up to 2S products; fp16 / bf16
+grad_w is compared after rounding the oracle to the same storage."""
+
+import pytest
+import torch
+
+import neural_shift_cuda_b200 as nsc
+from oracle import nsc_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _grads(x, w, sh, gU, gZ, dev):
+    xc = x.to(dev).requires_grad_(True)
+    wc = w.to(dev).requires_grad_(True)
+    U, Z = nsc.accumulate_uz(xc, wc, sh)
+    gx, gw = torch.autograd.grad((U, Z), (xc, wc), (gU.to(dev), gZ.to(dev)))
+    return gx.cpu(), gw.cpu()
+
+
+@pytest.mark.parametrize("dtype,C,Cw,H,W,table", [
+    (torch.float16, 3, 1, 40, 256, ("half", 10)),     # configs[4] family
+    (torch.float32, 3, 1, 23, 132, ("half", 3)),      # partial tiles
+    (torch.bfloat16, 1, 1, 17, 64, ("half", 5)),
+    (torch.float32, 2, 2, 20, 36, ("half", 2)),       # per-channel weights
+    (torch.float16, 3, 3, 9, 40, ("window", 4)),      # full window, H < halo
+    (torch.float32, 1, 1, 30, 128, ("window", 6)),
+    (torch.float32, 3, 1, 12, 16, ("half", 12)),      # image narrower than a tile
+])
+def test_tiled_grad_w_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, table):
+    torch.manual_seed(H + W)
+    kind, R = table
+    rows = O.halfplane_shifts(R) if kind == "half" else O.window_shifts(R)
+    sh = torch.tensor(rows)
+    S = len(rows)
+    B = 2
+    x = torch.rand(B, C, H, W).to(dtype)
+    w = torch.rand(S * B, Cw, H, W).to(dtype)
+    gU, gZ = torch.randn(B, C, H, W), torch.randn(B, C, H, W)
+    gx, gw = _grads(x, w, sh, gU, gZ, cuda)
+    gxr, gwr = O.accumulate_uz_backward(x, w, gU, gZ, sh)
+    if dtype == torch.float32:
+        torch.testing.assert_close(gx, gxr, rtol=1e-4, atol=1e-4)
+    else:   # grad_x is returned in x's storage dtype
+        torch.testing.assert_close(gx.float(), gxr.to(dtype).float(), rtol=1e-2, atol=1e-2)
+    if dtype == torch.float32:
+        torch.testing.assert_close(gw, gwr, rtol=1e-4, atol=1e-4)
+    else:   # one rounding to the weight storage: within one ulp of it
+        torch.testing.assert_close(gw.float(), gwr.to(dtype).float(),
+                                   rtol=1e-2, atol=1e-2)
+    monkeypatch.setenv("NSC_DISABLE_FAST", "1")
+    gx2, gw2 = _grads(x, w, sh, gU, gZ, cuda)
+    torch.testing.assert_close(gw.float(), gw2.float(),
+                               rtol=1e-4 if dtype == torch.float32 else 1e-2,
+                               atol=1e-4 if dtype == torch.float32 else 1e-2)
