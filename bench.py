@@ -323,6 +323,12 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic,
+                         "traffic_source": ("from profile: dram__bytes_read.sum + "
+                                            "dram__bytes_write.sum of one ncu capture of "
+                                            "this kernel at this size, committed in "
+                                            "profiles/accumulate_uz_fwd_8192x8192_S221.md "
+                                            "(not measured in this run)")
+                         if traffic is not None else None,
                          "kernel_ms": kern_ms, "algorithmic_bytes": alg,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
                          if peaks else "fallback 6650 GB/s"},

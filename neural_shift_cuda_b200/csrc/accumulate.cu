@@ -454,6 +454,8 @@ nsc_status acc_bwd(const void* x, int xd, const void* w, int wd, int64_t Cw,
     // grad_w by the tiled correlation kernel when it takes the call; the
     // general kernel then computes grad_x only
     const bool gw_done = acc_gw_fast(x, xd, wd, Cw, B, C, H, W, st, gU, gZ, gw, stream);
+    if (gw_done && acc_gx_fast(w, xd, wd, Cw, B, C, H, W, st, gU, gx, stream))
+        return check_launch("accumulate_uz_backward");
     return with_types("accumulate_uz_backward", xd, wd, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;

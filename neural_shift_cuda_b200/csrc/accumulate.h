@@ -35,6 +35,12 @@ bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C
                  int64_t H, int64_t W, const ShiftTable& st, const void* gU,
                  const void* gZ, void* gw, cudaStream_t stream);
 
+// Tiled grad_x of accumulate_uz (same conditions; grad_x fp32); false when
+// it declines.
+bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C,
+                 int64_t H, int64_t W, const ShiftTable& st, const void* gU, void* gx,
+                 cudaStream_t stream);
+
 // Why the last acc_fwd_fast call on this thread declined ("" if it ran).
 const char* fast_decline_reason();
 

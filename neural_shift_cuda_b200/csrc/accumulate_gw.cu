@@ -21,6 +21,7 @@
 // (shift, thread) writes grad_w.
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 
 #include "nsc_common.cuh"
 #include "nsc_host.h"
@@ -199,6 +200,144 @@ acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
     }
 }
 
+// 4 weights of plane `ws` at image row `row`, columns c0 .. c0 + 3 (c0 may
+// be negative or reach past W: circular), as fp32.  OFF = c0 mod 4 is a
+// compile-time fact of the caller (c0 = thread column - dy); interior
+// threads use one or two aligned 8-byte loads.
+template <typename T, int OFF>
+__device__ __forceinline__ void load_w4(float (&d)[V], const T* ws, int64_t row,
+                                        int64_t c0, int64_t W) {
+    const T* r = ws + row * W;
+    if (sizeof(T) == 2 && c0 >= 0 && c0 + 8 <= W) {
+        const int64_t a = c0 - OFF;                 // multiple of 4
+        T e[8];
+        *reinterpret_cast<uint2*>(e) = __ldg(reinterpret_cast<const uint2*>(r + a));
+        if constexpr (OFF != 0)
+            *reinterpret_cast<uint2*>(e + 4) = __ldg(reinterpret_cast<const uint2*>(r + a + 4));
+#pragma unroll
+        for (int i = 0; i < V; ++i) d[i] = to_f(e[OFF + i]);
+    } else if (sizeof(T) == 4 && OFF == 0 && c0 >= 0 && c0 + 4 <= W) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(r + c0));
+        d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            int64_t c = c0 + i;
+            while (c < 0) c += W;
+            while (c >= W) c -= W;
+            d[i] = to_f(__ldg(r + c));
+        }
+    }
+}
+
+// grad_x of accumulate_uz (the transpose of the forward operator):
+//   gx_c(q) = sum_s w_s(q - d) gU_c(q - d)                  (circular)
+//           + inv [q + d inside] w_s(q) gU_c(q + d)
+// Same tile and thread layout as the grad_w kernel.  grad_U is staged twice
+// with its halo: circular (first term) and zero outside the image (second
+// term's inside test).  Per dx row each thread holds the grad_U windows of
+// its 4 pixels for every channel; per shift it reads its 4 weights at q
+// and the 4 at q - d straight from global memory (neighbouring tiles read
+// the same rows, so the re-reads are L2 hits) and accumulates in registers.
+template <typename T, int NC, int DYMIN, int DYMAX>
+__global__ void __launch_bounds__(NT)
+acc_gx_kernel(const T* __restrict__ w, const float* __restrict__ gU,
+              float* __restrict__ gx, const GwTable tab, const GwGeo g) {
+    constexpr int NDY = DYMAX - DYMIN + 1;
+    constexpr int NWIN = NDY + V - 1;
+    extern __shared__ __align__(16) float smem_f[];
+    const int XH = g.XH, XW = g.XW, plane = XH * XW;
+    float* sc = smem_f;                 // [NC][XH][XW] grad_U, circular
+    float* sm = sc + NC * plane;        // [NC][XH][XW] grad_U, zero outside
+    const int Rx = tab.Rx;
+    const int64_t HW = g.H * g.W;
+    const int64_t cgroups = g.Cw == 1 ? 1 : g.C;
+    const int64_t grp = blockIdx.y;
+    const int64_t b = grp / cgroups;
+    const int64_t c0 = g.Cw == 1 ? 0 : grp % cgroups;
+    const int ty = blockIdx.x / g.tiles_x, tx = blockIdx.x - ty * g.tiles_x;
+    const int64_t h0 = static_cast<int64_t>(ty) * TH, w0 = static_cast<int64_t>(tx) * TW;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = warp; r < XH; r += NT / 32) {
+        const int64_t gh = h0 - Rx + r;
+        const bool rin = gh >= 0 && gh < g.H;
+        int64_t hw = gh % g.H;
+        if (hw < 0) hw += g.H;
+        for (int cc = lane; cc < XW; cc += 32) {
+            const int e = r * XW + cc;
+            const int64_t gc = w0 - g.CO + cc;
+            const bool in = rin && gc >= 0 && gc < g.W;
+            int64_t cw = gc;
+            while (cw < 0) cw += g.W;
+            while (cw >= g.W) cw -= g.W;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int64_t pl = (b * g.C + c0 + c) * HW;
+                const float v = gU[pl + hw * g.W + cw];
+                sc[c * plane + e] = v;
+                sm[c * plane + e] = in ? v : 0.f;
+            }
+        }
+    }
+    __syncthreads();
+
+    const int tr = threadIdx.x / TPR, tc = threadIdx.x % TPR;
+    const int64_t h = h0 + tr, wc0 = w0 + tc * V;
+    if (h >= g.H || wc0 >= g.W) return;
+    const int own = (tr + Rx) * XW + g.CO + tc * V;
+    const T* const wbase = w + (b * g.Cw + (g.Cw == 1 ? 0 : c0)) * HW;
+    const int64_t pstride = g.B * g.Cw * HW;
+    float acc[NC][V];
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[c][i] = 0.f;
+
+    for (int dx = -Rx; dx <= Rx; ++dx) {
+        const uint32_t pres = static_cast<uint32_t>(tab.present[dx + MAXR] >> (DYMIN + MAXR));
+        if (!pres) continue;
+        const uint32_t invm = static_cast<uint32_t>(tab.inv[dx + MAXR] >> (DYMIN + MAXR));
+        int64_t hm = (h - dx) % g.H;            // row of q - d, circular
+        if (hm < 0) hm += g.H;
+        // windows: A = grad_U(q - d) over dy (circular), B = grad_U(q + d) (masked)
+        float wa[NC][NWIN], wb[NC][NWIN];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            load_row<NWIN, false>(wa[c], sc + c * plane + own - dx * XW - DYMAX);
+            load_row<NWIN, DYMIN % 4 == 0>(wb[c], sm + c * plane + own + dx * XW + DYMIN);
+        }
+        sfor<0, NDY>([&](auto jc) {
+            constexpr int j = decltype(jc)::value;
+            constexpr int dy = DYMIN + j;
+            if (!((pres >> j) & 1u)) return;
+            const int s = tab.s[dx + MAXR][dy + MAXR];
+            const T* ws = wbase + s * pstride;
+            float wm[V];
+            load_w4<T, ((-dy) % 4 + 4) % 4>(wm, ws, hm, wc0 - dy, g.W);
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int i = 0; i < V; ++i)
+                    acc[c][i] = fmaf(wm[i], wa[c][i - dy + DYMAX], acc[c][i]);
+            if ((invm >> j) & 1u) {
+                float wq[V];
+                load_w4<T, 0>(wq, ws, h, wc0, g.W);
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+#pragma unroll
+                    for (int i = 0; i < V; ++i)
+                        acc[c][i] = fmaf(wq[i], wb[c][j + i], acc[c][i]);
+            }
+        });
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        float* dst = gx + (b * g.C + c0 + c) * HW + h * g.W + wc0;
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
+    }
+}
+
 template <typename T, int NC, int LO, int HI>
 bool launch(const void* x, const void* gU, const void* gZ, void* gw, const GwTable& tab,
             const GwGeo& g, size_t smem, dim3 grid, cudaStream_t stream) {
@@ -225,6 +364,32 @@ bool by_range(int lo, int hi, const void* x, const void* gU, const void* gZ, voi
     return false;
 }
 
+template <typename T, int NC, int LO, int HI>
+bool launch_gx(const void* w, const void* gU, void* gx, const GwTable& tab,
+               const GwGeo& g, size_t smem, dim3 grid, cudaStream_t stream) {
+    auto k = acc_gx_kernel<T, NC, LO, HI>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    k<<<grid, NT, smem, stream>>>(static_cast<const T*>(w), static_cast<const float*>(gU),
+                                  static_cast<float*>(gx), tab, g);
+    return true;
+}
+
+template <typename T, int NC>
+bool gx_by_range(int lo, int hi, const void* w, const void* gU, void* gx,
+                 const GwTable& tab, const GwGeo& g, size_t smem, dim3 grid,
+                 cudaStream_t st) {
+#define NSC_GX(L, H) \
+    if (lo == L && hi == H) return launch_gx<T, NC, L, H>(w, gU, gx, tab, g, smem, grid, st);
+    NSC_GX(0, 2) NSC_GX(0, 4) NSC_GX(0, 6) NSC_GX(0, 8) NSC_GX(0, 10) NSC_GX(0, 12)
+    NSC_GX(-4, 4) NSC_GX(-6, 6)
+#undef NSC_GX
+    return false;
+}
+
 inline bool dispatch(int xd, int NC, int lo, int hi, const void* x, const void* gU,
                      const void* gZ, void* gw, const GwTable& tab, const GwGeo& g,
                      size_t smem, dim3 grid, cudaStream_t st) {
@@ -242,52 +407,68 @@ inline bool dispatch(int xd, int NC, int lo, int hi, const void* x, const void* 
 
 // Tiled grad_w; returns false (nothing launched) when the call is outside
 // what it handles.
-bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C,
-                 int64_t H, int64_t W, const ShiftTable& st, const void* gU,
-                 const void* gZ, void* gw, cudaStream_t stream) {
+namespace {
+
+// Table and geometry shared by the tiled grad_w and grad_x kernels; false
+// when the call is outside what they handle.
+bool prepare(int xd, int wd, int64_t Cw, int64_t B, int64_t C, int64_t H, int64_t W,
+             const ShiftTable& st, std::initializer_list<const void*> ptrs,
+             gwk::GwTable* tab, gwk::GwGeo* g, int* lo, int* hi) {
     using namespace gwk;
     if (std::getenv("NSC_DISABLE_FAST")) return false;
     if (xd != wd || xd == NSC_F64) return false;
     if (!(Cw == C || (Cw == 1 && (C == 1 || C == 3)))) return false;
     if (W % V != 0) return false;
-    for (const void* p : {x, gU, gZ, static_cast<const void*>(gw)})
+    for (const void* p : ptrs)
         if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
     if (B * (Cw == 1 ? 1 : C) > 65535) return false;
-    GwTable tab;
-    std::memset(&tab, 0, sizeof(tab));
-    for (auto& r : tab.s)
+    std::memset(tab, 0, sizeof(*tab));
+    for (auto& r : tab->s)
         for (auto& v : r) v = -1;
     int dymin = MAXR, dymax = -MAXR, rx = 0;
     for (int s = 0; s < st.S; ++s) {
         const int dx = st.dx[s], dy = st.dy[s];
         if (dx < -MAXR || dx > MAXR || dy < -MAXR || dy > MAXR) return false;
         if (!st.has_fwd(s) || st.has_per(s)) return false;   // transposed / periodic rows
-        if (tab.s[dx + MAXR][dy + MAXR] >= 0) return false;  // repeated shift
-        tab.s[dx + MAXR][dy + MAXR] = static_cast<int16_t>(s);
-        tab.present[dx + MAXR] |= 1ull << (dy + MAXR);
-        if (st.has_inv(s)) tab.inv[dx + MAXR] |= 1ull << (dy + MAXR);
+        if (tab->s[dx + MAXR][dy + MAXR] >= 0) return false; // repeated shift
+        tab->s[dx + MAXR][dy + MAXR] = static_cast<int16_t>(s);
+        tab->present[dx + MAXR] |= 1ull << (dy + MAXR);
+        if (st.has_inv(s)) tab->inv[dx + MAXR] |= 1ull << (dy + MAXR);
         dymin = dy < dymin ? dy : dymin;
         dymax = dy > dymax ? dy : dymax;
         rx = (dx < 0 ? -dx : dx) > rx ? (dx < 0 ? -dx : dx) : rx;
     }
-    tab.Rx = rx;
-    int lo, hi;
+    tab->Rx = rx;
     if (dymin >= 0) {
-        lo = 0;
-        hi = dymax <= 2 ? 2 : dymax <= 4 ? 4 : dymax <= 6 ? 6 : dymax <= 8 ? 8
-             : dymax <= 10 ? 10 : dymax <= 12 ? 12 : -1;
+        *lo = 0;
+        *hi = dymax <= 2 ? 2 : dymax <= 4 ? 4 : dymax <= 6 ? 6 : dymax <= 8 ? 8
+              : dymax <= 10 ? 10 : dymax <= 12 ? 12 : -1;
     } else {
         const int k = dymax > -dymin ? dymax : -dymin;
-        lo = k <= 4 ? -4 : k <= 6 ? -6 : 1;
-        hi = -lo;
+        *lo = k <= 4 ? -4 : k <= 6 ? -6 : 1;
+        *hi = -*lo;
     }
-    if (hi < 0 || lo > 0) return false;
-    GwGeo g{};
-    g.B = B; g.C = C; g.H = H; g.W = W; g.Cw = Cw;
-    g.tiles_x = static_cast<int32_t>((W + TW - 1) / TW);
-    g.tiles_y = static_cast<int32_t>((H + TH - 1) / TH);
-    if (static_cast<int64_t>(g.tiles_x) * g.tiles_y >= (1LL << 31)) return false;
-    g.XH = TH + 2 * rx;
+    if (*hi < 0 || *lo > 0) return false;
+    *g = GwGeo{};
+    g->B = B; g->C = C; g->H = H; g->W = W; g->Cw = Cw;
+    g->tiles_x = static_cast<int32_t>((W + TW - 1) / TW);
+    g->tiles_y = static_cast<int32_t>((H + TH - 1) / TH);
+    if (static_cast<int64_t>(g->tiles_x) * g->tiles_y >= (1LL << 31)) return false;
+    g->XH = TH + 2 * rx;
+    return true;
+}
+
+}  // namespace
+
+bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C,
+                 int64_t H, int64_t W, const ShiftTable& st, const void* gU,
+                 const void* gZ, void* gw, cudaStream_t stream) {
+    using namespace gwk;
+    GwTable tab;
+    GwGeo g;
+    int lo, hi;
+    if (!prepare(xd, wd, Cw, B, C, H, W, st, {x, gU, gZ, gw}, &tab, &g, &lo, &hi))
+        return false;
     g.CO = (-lo + 3) / 4 * 4;                 // 16-byte aligned own pixels
     g.XW = (g.CO + TW + hi + 3) / 4 * 4;
     const int NC = Cw == 1 ? static_cast<int>(C) : 1;
@@ -296,6 +477,33 @@ bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C
     const dim3 grid(static_cast<unsigned>(g.tiles_x * g.tiles_y),
                     static_cast<unsigned>(B * (Cw == 1 ? 1 : C)));
     return gwk::dispatch(xd, NC, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, stream);
+}
+
+bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C,
+                 int64_t H, int64_t W, const ShiftTable& st, const void* gU, void* gx,
+                 cudaStream_t stream) {
+    using namespace gwk;
+    GwTable tab;
+    GwGeo g;
+    int lo, hi;
+    if (!prepare(xd, wd, Cw, B, C, H, W, st, {w, gU, gx}, &tab, &g, &lo, &hi))
+        return false;
+    const int K = hi > -lo ? hi : -lo;        // windows reach q - d and q + d
+    g.CO = (K + 3) / 4 * 4;
+    g.XW = (g.CO + TW + K + 3) / 4 * 4;
+    const int NC = Cw == 1 ? static_cast<int>(C) : 1;
+    const size_t smem = static_cast<size_t>(2 * NC) * g.XH * g.XW * sizeof(float);
+    if (smem > 227u * 1024u) return false;
+    const dim3 grid(static_cast<unsigned>(g.tiles_x * g.tiles_y),
+                    static_cast<unsigned>(B * (Cw == 1 ? 1 : C)));
+    if (xd == NSC_F16)
+        return NC == 3 ? gx_by_range<__half, 3>(lo, hi, w, gU, gx, tab, g, smem, grid, stream)
+                       : gx_by_range<__half, 1>(lo, hi, w, gU, gx, tab, g, smem, grid, stream);
+    if (xd == NSC_BF16)
+        return NC == 3 ? gx_by_range<__nv_bfloat16, 3>(lo, hi, w, gU, gx, tab, g, smem, grid, stream)
+                       : gx_by_range<__nv_bfloat16, 1>(lo, hi, w, gU, gx, tab, g, smem, grid, stream);
+    return NC == 3 ? gx_by_range<float, 3>(lo, hi, w, gU, gx, tab, g, smem, grid, stream)
+                   : gx_by_range<float, 1>(lo, hi, w, gU, gx, tab, g, smem, grid, stream);
 }
 
 }  // namespace nsc

@@ -1,5 +1,5 @@
-"""GPU parity of the accumulate_uz backward with the tiled grad_w kernel
-(csrc/accumulate_gw.cu) against the oracle, and against the general
+"""GPU parity of the accumulate_uz backward with the tiled grad_w and
+grad_x kernels (csrc/accumulate_gw.cu) against the oracle, and against the general
 kernel (NSC_DISABLE_FAST=1 declines every tiled path).  Tolerance: fp32
 rtol/atol 1e-4 on gradients of sums of up to 2S products; fp16 / bf16
 grad_w is compared after rounding the oracle to the same storage."""
@@ -53,6 +53,8 @@ def test_tiled_grad_w_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, tabl
                                    rtol=1e-2, atol=1e-2)
     monkeypatch.setenv("NSC_DISABLE_FAST", "1")
     gx2, gw2 = _grads(x, w, sh, gU, gZ, cuda)
+    tol = 1e-4 if dtype == torch.float32 else 1e-2   # fp16 / bf16: one rounding apart
+    torch.testing.assert_close(gx.float(), gx2.float(), rtol=tol, atol=tol)
     torch.testing.assert_close(gw.float(), gw2.float(),
                                rtol=1e-4 if dtype == torch.float32 else 1e-2,
                                atol=1e-4 if dtype == torch.float32 else 1e-2)
