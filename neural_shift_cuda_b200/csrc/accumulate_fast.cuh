@@ -483,6 +483,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         }
         for (int i = 0; i < 4; ++i) mbar_init(&tile_full[i], 1);
         abort_flag = 0;
+        (&abort_flag)[1] = static_cast<int>(g.wait_budget);   // read by the slow waits
         fence_mbar_init();
     }
     __syncthreads();
@@ -710,7 +711,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 constexpr int dy = decltype(dyc)::value;
                 if (pos == 0)
                     mbar_wait32_ab(full32 + 8 * stage, phase, timeouts,
-                                   (volatile int*)&abort_flag, g.wait_budget);
+                                   (volatile int*)&abort_flag);
                 const uint32_t sp = after(stp) + pos * g.plane_bytes;
                 constexpr int mo = dy > 0 ? align_up(dy, V) : 0;
                 uint32_t wv[V / EPW];

@@ -106,11 +106,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // before any suspension: once one thread gave up, the others return at once
 // instead of each running out its own limit.  The fast path (phase already
 // complete) is a single try_wait.
+// abort_flag[1] holds the wait budget (hinted sleeps) of the launch.
 static __device__ __noinline__ bool mbar_wait32_slow(uint32_t bar, uint32_t parity,
                                               unsigned int* timeouts,
-                                              volatile int* abort_flag,
-                                              uint32_t budget) {
+                                              volatile int* abort_flag) {
     if (*abort_flag) return false;
+    const uint32_t budget = static_cast<uint32_t>(abort_flag[1]);
     for (uint32_t i = 0; i < budget; ++i) {
         if (mbar_try_wait_sleep32(bar, parity)) return true;
         if ((i & 63u) == 63u && *abort_flag) return false;
@@ -121,10 +122,9 @@ static __device__ __noinline__ bool mbar_wait32_slow(uint32_t bar, uint32_t pari
 }
 __device__ __forceinline__ bool mbar_wait32_ab(uint32_t bar, uint32_t parity,
                                                unsigned int* timeouts,
-                                               volatile int* abort_flag,
-                                               uint32_t budget = kSleepWaits) {
+                                               volatile int* abort_flag) {
     if (mbar_try_wait32(bar, parity)) return true;
-    return mbar_wait32_slow(bar, parity, timeouts, abort_flag, budget);
+    return mbar_wait32_slow(bar, parity, timeouts, abort_flag);
 }
 __device__ __forceinline__ bool mbar_wait32(uint32_t bar, uint32_t parity,
                                             unsigned int* timeouts) {
