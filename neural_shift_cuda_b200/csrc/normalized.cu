@@ -362,8 +362,7 @@ nsc_status nsc_normalized_accumulate_uz_fwd(
     if (!x || !w || !D || !log_C)
         return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
     cudaStream_t sm = as_stream(stream);
-    if (!getenv("NSC_NORM_TMA") &&
-        norm_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, st,
+    if (norm_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, st,
                       log_weights ? 1 : 0, D, log_C, invalid_flag, sm))
         return check_launch(op);
     // tables with mirror terms: the TMA-tiled kernel in its normalized modes

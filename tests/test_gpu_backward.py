@@ -29,6 +29,10 @@ def _grads(x, w, sh, gU, gZ, dev):
     (torch.float16, 3, 3, 9, 40, ("window", 4)),      # full window, H < halo
     (torch.float32, 1, 1, 30, 128, ("window", 6)),
     (torch.float32, 3, 1, 12, 16, ("half", 12)),      # image narrower than a tile
+    (torch.float16, 3, 1, 12, 16, ("half", 12)),      # weight rows wrap twice
+    (torch.bfloat16, 3, 1, 19, 136, ("window", 6)),   # negative dy
+    (torch.float16, 1, 1, 33, 200, ("half", 4)),      # partial tiles
+    (torch.float16, 1, 1, 9, 12, ("half", 2)),
 ])
 def test_tiled_grad_w_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, table):
     torch.manual_seed(H + W)
