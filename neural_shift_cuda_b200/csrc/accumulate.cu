@@ -188,6 +188,59 @@ acc_edges2_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
     }
 }
 
+// Periodic mirror rows on the tiled path: the tile kernel treats every
+// mirror term as masked (its weight boxes are zero outside the image), which
+// is the periodic term wherever p - d stays inside the image.  This kernel
+// adds the remaining wrapped terms -- w_s((p - d) mod (H, W)) x((p - d) mod)
+// for periodic rows whose p - d leaves the image -- which exist only on the
+// R-pixel border band.
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(256)
+acc_per_fix_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                   typename Acc<TX>::type* __restrict__ U,
+                   typename Acc<TX>::type* __restrict__ Z, const ShiftTable st,
+                   int64_t B, int64_t C, int64_t H, int64_t W, int64_t Cw, int64_t R,
+                   int64_t nb, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= nb) return;
+    int64_t h, wcol;
+    border_pixel(i, H, W, R, h, wcol);
+    const int64_t plane = H * W;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    for (int64_t g = blockIdx.y; g < groups; g += gridDim.y) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const TX* xb = x + (b * C + c0) * plane;
+        A u[NC], z = A(0);
+#pragma unroll
+        for (int k = 0; k < NC; ++k) u[k] = A(0);
+        for (int s = 0; s < st.S; ++s) {
+            if (!st.has_per(s)) continue;
+            int64_t hm = h - st.dx[s], wm = wcol - st.dy[s];
+            if (inb(hm, H) && inb(wm, W)) continue;     // counted by the tile kernel
+            hm = wrap1(hm, H);
+            wm = wrap1(wm, W);
+            const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
+            const A mv = ldg_acc<TW, A>(ws + hm * W + wm);
+#pragma unroll
+            for (int k = 0; k < NC; ++k)
+                if (k < nc) u[k] += mv * ldg_acc<TX, A>(xb + k * plane + hm * W + wm);
+            z += mv;
+        }
+        const int64_t ob = (b * C + c0) * plane + h * W + wcol;
+#pragma unroll
+        for (int k = 0; k < NC; ++k)
+            if (k < nc) {
+                U[ob + k * plane] += u[k];
+                Z[ob + k * plane] += z;
+            }
+    }
+}
+
 // U/Z += neighbour strips; one thread per strip element and strip.
 template <typename A>
 __global__ void __launch_bounds__(256)
@@ -402,6 +455,28 @@ nsc_status acc_fwd_generic(const void* x, int xd, const void* w, int wd,
 }
 
 
+nsc_status acc_per_fix(const void* x, int xd, const void* w, int wd, int64_t Cw,
+                       int64_t B, int64_t C, int64_t H, int64_t W, const ShiftTable& st,
+                       void* U, void* Z, cudaStream_t stream) {
+    const int64_t R = st.R;
+    const int64_t nb = border_count(H, W, R);
+    return with_types("accumulate_uz", xd, wd, [&](auto tx, auto tw) {
+        using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        using A = typename Acc<TX>::type;
+        with_nc(C, Cw, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, Cw, NC);
+            const dim3 grid(grid_1d(nb, 256),
+                            static_cast<unsigned>(groups < 65535 ? groups : 65535));
+            acc_per_fix_kernel<TX, TW, NC><<<grid, 256, 0, stream>>>(
+                static_cast<const TX*>(x), static_cast<const TW*>(w), static_cast<A*>(U),
+                static_cast<A*>(Z), st, B, C, H, W, Cw, R, nb, groups);
+        });
+        return check_launch("accumulate_uz");
+    });
+}
+
 nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
                      int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t row0,
                      int64_t Hg, const ShiftTable& st, void* top, void* bot,
@@ -515,8 +590,12 @@ nsc_status nsc_accumulate_uz_fwd(const void* x, int x_dtype, const void* w,
     if (!x || !w || !U || !Z)
         return fail(NSC_ERR_INVALID_ARG, "accumulate_uz: NULL tensor pointer");
     if (acc_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0, 1,
-                     st, U, Z, as_stream(stream)))
+                     st, U, Z, as_stream(stream))) {
+        if (st.any_per)   // wrapped periodic mirror terms of the border band
+            return acc_per_fix(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, st, U, Z,
+                               as_stream(stream));
         return check_launch("accumulate_uz");
+    }
     if (std::getenv("NSC_REQUIRE_FAST"))
         return fail(NSC_ERR_INVALID_ARG,
                     "accumulate_uz: the tiled path declined this call "

@@ -41,6 +41,12 @@ bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C
                  int64_t H, int64_t W, const ShiftTable& st, const void* gU, void* gx,
                  cudaStream_t stream);
 
+// After a tiled forward (mode 0) of a table with periodic mirror rows: add
+// the wrapped mirror terms the tile kernel leaves out (border band only).
+nsc_status acc_per_fix(const void* x, int xd, const void* w, int wd, int64_t Cw,
+                       int64_t B, int64_t C, int64_t H, int64_t W, const ShiftTable& st,
+                       void* U, void* Z, cudaStream_t stream);
+
 // Why the last acc_fwd_fast call on this thread declined ("" if it ran).
 const char* fast_decline_reason();
 

@@ -92,7 +92,11 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     if (h_begin < 0 || h_begin > h_end || h_end > Hout) DECLINE("row range");
     if (mode != 0 && !wrap) DECLINE("normalized modes take full images only");
     if (std::getenv("NSC_DISABLE_FAST")) DECLINE("disabled by NSC_DISABLE_FAST");
-    if (st.any_per) DECLINE("periodic mirror rows");
+    if (st.any_tr) DECLINE("transposed rows");
+    // periodic mirror rows: the tile kernel computes them as masked rows and
+    // the caller adds the wrapped terms of the border band
+    if (st.any_per && (!wrap || Hout <= 2 * st.R || W <= 2 * st.R))
+        DECLINE("periodic mirror rows outside a full image larger than 2R");
     if (xd != wd || (xd != NSC_F16 && xd != NSC_BF16 && xd != NSC_F32)) DECLINE("dtype");
     const int es = xd == NSC_F32 ? 4 : 2;
     const int V = 16 / es;

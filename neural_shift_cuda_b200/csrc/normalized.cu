@@ -144,6 +144,74 @@ norm_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
     if (seen_invalid && invalid) atomicOr(invalid, 1);
 }
 
+// Periodic mirror rows on the tiled path (see acc_per_fix_kernel): the
+// wrapped mirror keys of the border band, normalised on their own and merged
+// into the tile kernel's (D, log_C):
+//   D = (D1 e^(L1 - M) + D2 e^(L2 - M)) / (e^(L1 - M) + e^(L2 - M)),
+//   L = M + log(e^(L1 - M) + e^(L2 - M)),  M = max(L1, L2).
+template <typename TX, typename TW, int NC>
+__global__ void __launch_bounds__(256)
+norm_per_fix_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                    typename Acc<TX>::type* __restrict__ D,
+                    typename Acc<TX>::type* __restrict__ L, const ShiftTable st,
+                    int64_t B, int64_t C, int64_t H, int64_t W, int64_t Cw, int64_t R,
+                    int logw, int64_t nb, int64_t groups) {
+    using A = typename Acc<TX>::type;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= nb) return;
+    int64_t h, wcol;
+    border_pixel(i, H, W, R, h, wcol);
+    const int64_t plane = H * W;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    for (int64_t g = blockIdx.y; g < groups; g += gridDim.y) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const TX* xb = x + (b * C + c0) * plane;
+        Online<A, NC> on;
+        on.init();
+        for (int s = 0; s < st.S; ++s) {
+            if (!st.has_per(s)) continue;
+            int64_t hm = h - st.dx[s], wm = wcol - st.dy[s];
+            if (inb(hm, H) && inb(wm, W)) continue;     // in the tile kernel's sums
+            hm = wrap1(hm, H);
+            wm = wrap1(wm, W);
+            const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
+            A xv[NC];
+#pragma unroll
+            for (int k = 0; k < NC; ++k)
+                xv[k] = (k < nc) ? ldg_acc<TX, A>(xb + k * plane + hm * W + wm) : A(0);
+            on.push(ldg_acc<TW, A>(ws + hm * W + wm), xv, logw);
+        }
+        if (!on.bad && on.m == neg_inf<A>()) continue;   // nothing wrapped here
+        const int64_t ob = (b * C + c0) * plane + h * W + wcol;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            if (k >= nc) continue;
+            A& d = D[ob + k * plane];
+            A& l = L[ob + k * plane];
+            if (on.bad || !(isfinite(on.m) && on.sz > A(0) && isfinite(on.sz)) || l != l) {
+                d = A(NAN);
+                l = A(NAN);
+                continue;
+            }
+            const A d2 = on.su[k] / on.sz;
+            const A l2 = (logw ? on.m : log_acc(on.m)) + log_acc(on.sz);
+            if (l == neg_inf<A>()) {
+                d = d2;
+                l = l2;
+                continue;
+            }
+            const A M = l > l2 ? l : l2;
+            const A a1 = exp_acc(l - M), a2 = exp_acc(l2 - M);
+            d = (d * a1 + d2 * a2) / (a1 + a2);
+            l = M + log_acc(a1 + a2);
+        }
+    }
+}
+
 template <typename A>
 __device__ __forceinline__ A as_log(A v, int logw) {
     if (logw) return v;
@@ -368,8 +436,27 @@ nsc_status nsc_normalized_accumulate_uz_fwd(
     // tables with mirror terms: the TMA-tiled kernel in its normalized modes
     if (!getenv("NSC_NORM_GENERIC") &&
         acc_fwd_fast(x, x_dtype, w, w_dtype, w_channels, B, C, H, W, H, 0, 1, st,
-                     D, log_C, sm, log_weights ? 1 : 2, invalid_flag))
-        return check_launch(op);
+                     D, log_C, sm, log_weights ? 1 : 2, invalid_flag)) {
+        if (!st.any_per) return check_launch(op);
+        // wrapped periodic mirror terms of the border band
+        return with_types(op, x_dtype, w_dtype, [&](auto tx, auto tw) {
+            using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
+            using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+            using A = typename Acc<TX>::type;
+            const int64_t R = st.R, nb = border_count(H, W, R);
+            with_nc(C, w_channels, [&](auto tag) {
+                constexpr int NC = decltype(tag)::value_nc;
+                const int64_t groups = n_groups(B, C, w_channels, NC);
+                const dim3 grid(grid_1d(nb, 256),
+                                static_cast<unsigned>(groups < 65535 ? groups : 65535));
+                norm_per_fix_kernel<TX, TW, NC><<<grid, 256, 0, sm>>>(
+                    static_cast<const TX*>(x), static_cast<const TW*>(w),
+                    static_cast<A*>(D), static_cast<A*>(log_C), st, B, C, H, W,
+                    w_channels, R, log_weights ? 1 : 0, nb, groups);
+            });
+            return check_launch(op);
+        });
+    }
     if (getenv("NSC_REQUIRE_FAST"))
         return fail(NSC_ERR_INVALID_ARG, "%s: tiled paths declined: %s; %s", op,
                     norm_fast_decline_reason(), fast_decline_reason());

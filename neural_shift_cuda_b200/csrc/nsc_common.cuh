@@ -87,6 +87,35 @@ __device__ __forceinline__ bool inb(int64_t i, int64_t n) {
     return i >= 0 && i < n;
 }
 
+// Pixel i of the border band of an H x W plane: the R rows at the top and
+// at the bottom, then the R columns at the left and right of the rows
+// between.  The band holds 2 R W + 2 R (H - 2 R) pixels (H, W > 2 R).
+__device__ __forceinline__ void border_pixel(int64_t i, int64_t H, int64_t W, int64_t R,
+                                             int64_t& h, int64_t& w) {
+    const int64_t strip = R * W;
+    if (i < strip) {
+        h = i / W;
+        w = i - h * W;
+        return;
+    }
+    i -= strip;
+    if (i < strip) {
+        const int64_t r = i / W;
+        h = H - R + r;
+        w = i - r * W;
+        return;
+    }
+    i -= strip;
+    const int64_t r2 = 2 * R;
+    const int64_t r = i / r2;
+    const int64_t k = i - r * r2;
+    h = R + r;
+    w = k < R ? k : W - r2 + k;
+}
+inline int64_t border_count(int64_t H, int64_t W, int64_t R) {
+    return 2 * R * W + 2 * R * (H - 2 * R);
+}
+
 // Grid helper: ceil-div clamped to an int grid dimension.
 inline unsigned grid_1d(int64_t n, int per_block, int64_t cap = (1LL << 31) - 1) {
     if (n <= 0) return 0;

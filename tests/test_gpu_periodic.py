@@ -128,3 +128,35 @@ def test_transpose_rejects_mirror_rows(cuda):
     w = torch.rand(3, 1, 6, 6, device=cuda)
     with pytest.raises(ValueError, match="forward-only"):
         nsc.accumulate_uz(x, w, torch.tensor(O.halfplane_shifts(1))[:3], transpose=True)
+
+
+@pytest.mark.parametrize("dtype,C,Cw,H,W,R", [
+    (torch.float32, 3, 1, 37, 64, 3),
+    (torch.float16, 3, 1, 40, 136, 5),
+    (torch.bfloat16, 1, 1, 23, 48, 2),
+    (torch.float32, 2, 2, 30, 36, 4),
+])
+def test_tiled_periodic_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, R):
+    """Periodic mirror rows on the tiled path (masked tile kernel plus the
+    wrapped terms of the border band): accumulate_uz and the normalized
+    reduction in log and positive modes, against the oracle."""
+    monkeypatch.setenv("NSC_REQUIRE_FAST", "1")
+    torch.manual_seed(H + W)
+    rows = O.halfplane_shifts(R)
+    sh = torch.tensor(rows)
+    S, B = len(rows), 2
+    x = torch.rand(B, C, H, W).to(dtype)
+    w = torch.rand(S * B, Cw, H, W).to(dtype)
+    per = _per(rows)
+    U, Z = nsc.accumulate_uz(x.to(cuda), w.to(cuda), sh, periodic_mirror=True)
+    Ur, Zr = O.accumulate_uz(x, w.expand(-1, C, -1, -1), per)
+    close(U, Ur, 1e-5)
+    close(Z, Zr, 1e-5)
+    for logw in (False, True):
+        k = (3.0 * torch.randn(S * B, Cw, H, W)).to(dtype) if logw else w
+        D, L = nsc.normalized_accumulate_uz(x.to(cuda), k.to(cuda), sh, log_weights=logw,
+                                            return_log_degree=True, validate=False,
+                                            periodic_mirror=True)
+        Dr, Lr = O.normalized_accumulate_uz(x, k.expand(-1, C, -1, -1), per, logw)
+        close(D, Dr, 1e-5)
+        close(L, Lr, 1e-5)
