@@ -21,7 +21,7 @@ namespace fast {
 
 template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT, int MODE>
 bool launch(const WMaps& maps, const void* x, void* U, void* Z,
-            const FastTable& tab, Geo g, unsigned int* timeouts,
+            const FastTable& tab, Geo g, GeoExt gx, unsigned int* timeouts,
             int* invalid, cudaStream_t stream);
 
 }  // namespace fast
@@ -48,9 +48,9 @@ int sm_count() {
 template <typename T, int NC, int M>
 bool by_bucket_m(bool exact, int K, const fast::WMaps& maps,
                  const void* x, void* U, void* Z, const fast::FastTable& tab,
-                 const fast::Geo& g, unsigned int* to, int* inv, cudaStream_t st) {
+                 const fast::Geo& g, const fast::GeoExt& gx, unsigned int* to, int* inv, cudaStream_t st) {
 #define NSC_B(A, B, E) \
-    return fast::launch<T, NC, A, B, E, M>(maps, x, U, Z, tab, g, to, inv, st)
+    return fast::launch<T, NC, A, B, E, M>(maps, x, U, Z, tab, g, gx, to, inv, st)
     if (exact) {
         switch (K) {
             case 2: NSC_B(0, 2, true);
@@ -73,10 +73,10 @@ bool by_bucket_m(bool exact, int K, const fast::WMaps& maps,
 template <typename T, int NC>
 bool by_bucket(int mode, bool exact, int K, const fast::WMaps& maps,
                const void* x, void* U, void* Z, const fast::FastTable& tab,
-               const fast::Geo& g, unsigned int* to, int* inv, cudaStream_t st) {
-    if (mode == 1) return by_bucket_m<T, NC, 1>(exact, K, maps, x, U, Z, tab, g, to, inv, st);
-    if (mode == 2) return by_bucket_m<T, NC, 2>(exact, K, maps, x, U, Z, tab, g, to, inv, st);
-    return by_bucket_m<T, NC, 0>(exact, K, maps, x, U, Z, tab, g, to, inv, st);
+               const fast::Geo& g, const fast::GeoExt& gx, unsigned int* to, int* inv, cudaStream_t st) {
+    if (mode == 1) return by_bucket_m<T, NC, 1>(exact, K, maps, x, U, Z, tab, g, gx, to, inv, st);
+    if (mode == 2) return by_bucket_m<T, NC, 2>(exact, K, maps, x, U, Z, tab, g, gx, to, inv, st);
+    return by_bucket_m<T, NC, 0>(exact, K, maps, x, U, Z, tab, g, gx, to, inv, st);
 }
 
 }  // namespace
@@ -221,20 +221,21 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     if (!wrap && x_off < rx) DECLINE("band halo");
 
     Geo g{};
+    GeoExt gx{};
     g.B = B; g.C = C; g.H = Hout; g.W = W; g.Cw = Cw;
     g.x_rows = x_rows; g.x_off = x_off; g.wrap = wrap;
     {
         int skip;
         unsigned budget;
         wait_fault_settings(&skip, &budget);
-        g.skip_copy = skip;
-        g.wait_budget = budget;
+        gx.skip_copy = skip;
+        gx.wait_budget = budget;
     }
     const int TW = TPR * V;
     g.tiles_x = static_cast<int32_t>((W + TW - 1) / TW);
-    g.hb0 = static_cast<int32_t>(h_begin);
-    g.hb1 = static_cast<int32_t>(h_end);
-    g.max_ctas = max_ctas;
+    gx.hb0 = static_cast<int32_t>(h_begin);
+    gx.hb1 = static_cast<int32_t>(h_end);
+    gx.max_ctas = max_ctas;
     g.tiles_y = static_cast<int32_t>((h_end - h_begin + TH - 1) / TH);
     g.groups = B * (Cw == 1 ? 1 : C);
     g.ntiles = g.groups * g.tiles_y * g.tiles_x;
@@ -262,13 +263,13 @@ bool acc_fwd_fast(const void* x, int xd, const void* w, int wd, int64_t Cw,
     (void)sm_count;
     const int m = mode;
     if (xd == NSC_F16)
-        return NC == 1 ? by_bucket<__half, 1>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream)
-                       : by_bucket<__half, 3>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream);
+        return NC == 1 ? by_bucket<__half, 1>(m, exact, K, maps, x, U, Z, tab, g, gx, to, invalid, stream)
+                       : by_bucket<__half, 3>(m, exact, K, maps, x, U, Z, tab, g, gx, to, invalid, stream);
     if (xd == NSC_BF16)
-        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream)
-                       : by_bucket<__nv_bfloat16, 3>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream);
-    return NC == 1 ? by_bucket<float, 1>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream)
-                   : by_bucket<float, 3>(m, exact, K, maps, x, U, Z, tab, g, to, invalid, stream);
+        return NC == 1 ? by_bucket<__nv_bfloat16, 1>(m, exact, K, maps, x, U, Z, tab, g, gx, to, invalid, stream)
+                       : by_bucket<__nv_bfloat16, 3>(m, exact, K, maps, x, U, Z, tab, g, gx, to, invalid, stream);
+    return NC == 1 ? by_bucket<float, 1>(m, exact, K, maps, x, U, Z, tab, g, gx, to, invalid, stream)
+                   : by_bucket<float, 3>(m, exact, K, maps, x, U, Z, tab, g, gx, to, invalid, stream);
 }
 
 int fast_sm_count() { return sm_count(); }

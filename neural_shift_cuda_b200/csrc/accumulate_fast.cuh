@@ -113,10 +113,6 @@ struct Geo {
     int32_t XH, XW;             // x halo tile
     int32_t col_border;         // W is not a multiple of the tile width
     int32_t nstage;             // weight ring depth
-    int32_t hb0, hb1;           // output rows computed: [hb0, hb1) of [0, H)
-    int32_t max_ctas;           // grid cap (0: one CTA per SM)
-    uint32_t wait_budget;       // hinted sleeps (~1 ms each) before a wait gives up
-    int32_t skip_copy;          // test hook: this copy index is never issued (-1: none)
     uint32_t plane_bytes;       // one plane of a weight box in shared memory
 };
 
@@ -125,12 +121,20 @@ struct Geo {
 // the ones the persistent CTAs work on at the same time -- form a compact
 // block, so the weight rows one tile's box shares with its upper, lower and
 // left neighbours are fetched by concurrently running CTAs and meet in L2.
+// Launch settings kept out of Geo (a separate kernel parameter).
+struct GeoExt {
+    int32_t hb0, hb1;           // output rows computed: [hb0, hb1) of [0, H)
+    int32_t max_ctas;           // grid cap (0: one CTA per SM)
+    uint32_t wait_budget;       // hinted sleeps (~1 ms each) before a wait gives up
+    int32_t skip_copy;          // test hook: this copy index is never issued (-1: none)
+};
+
 struct TileId {
     int64_t b, grp;
     int h0, w0;
 };
 
-__device__ __forceinline__ TileId decode_tile(int64_t tile, const Geo& g, int TW,
+__device__ __forceinline__ TileId decode_tile(int64_t tile, const Geo& g, int hb0, int TW,
                                               int64_t cgroups) {
     const int64_t per = static_cast<int64_t>(g.tiles_x) * g.tiles_y;
     const int64_t grp = tile / per;
@@ -145,7 +149,7 @@ __device__ __forceinline__ TileId decode_tile(int64_t tile, const Geo& g, int TW
     TileId id;
     id.grp = grp;
     id.b = grp / cgroups;
-    id.h0 = g.hb0 + static_cast<int>(ty) * TH;
+    id.h0 = hb0 + static_cast<int>(ty) * TH;
     id.w0 = static_cast<int>(tx) * TW;
     return id;
 }
@@ -440,7 +444,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                 float* __restrict__ U, float* __restrict__ Zo, const FastTable tab,
                 const Geo g, unsigned int* timeouts,
-                unsigned long long* __restrict__ ticket, int* __restrict__ invalid) {
+                unsigned long long* __restrict__ ticket, int* __restrict__ invalid,
+                const GeoExt gx) {
     // modes 1 / 2: U receives D and Zo receives log_C
     constexpr int V = 16 / static_cast<int>(sizeof(T));
     constexpr int EPW = 4 / static_cast<int>(sizeof(T));   // elements per word
@@ -483,7 +488,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         }
         for (int i = 0; i < 4; ++i) mbar_init(&tile_full[i], 1);
         abort_flag = 0;
-        (&abort_flag)[1] = static_cast<int>(g.wait_budget);   // read by the slow waits
+        (&abort_flag)[1] = static_cast<int>(gx.wait_budget);   // read by the slow waits
         fence_mbar_init();
     }
     __syncthreads();
@@ -510,7 +515,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
             const int64_t tile = *(volatile int64_t*)&tile_ring[k & 3];
             if (tile < 0) break;
             fetch(k + 2);
-            const TileId id = decode_tile(tile, g, TW, cgroups);
+            const TileId id = decode_tile(tile, g, gx.hb0, TW, cgroups);
             const int64_t b = id.b;
             const int64_t wc = (g.Cw == 1) ? 0 : id.grp % cgroups;
             const int h0 = id.h0, w0 = id.w0;
@@ -521,13 +526,13 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                     const int len = (e >> kLenShift) & 7;
                     if (e < 0 || len == 0) continue;
                     const int s = e & kSMask;
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, timeouts, g.wait_budget) ||
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, timeouts, gx.wait_budget) ||
                         *(volatile int*)&abort_flag) {
                         aborted = true;
                         *(volatile int*)&abort_flag = 1;
                         break;
                     }
-                    if (static_cast<int32_t>(it) == g.skip_copy) {
+                    if (static_cast<int32_t>(it) == gx.skip_copy) {
                         // test hook: leave this stage's copy unissued, so the
                         // consumers' bounded waits on it give up
                         ++it;
@@ -553,8 +558,8 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
         // flight.  Wait (bounded) for the last NSTAGE loads to land.
         const uint32_t n = it < static_cast<uint32_t>(NSTAGE) ? it : NSTAGE;
         for (uint32_t j = it - n; j < it; ++j)
-            if (static_cast<int32_t>(j) != g.skip_copy)
-                mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts, g.wait_budget);
+            if (static_cast<int32_t>(j) != gx.skip_copy)
+                mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1u, timeouts, gx.wait_budget);
         return;
     }
 
@@ -592,7 +597,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                  col0 + V <= g.W;
     };
     auto issue_x = [&](int64_t tile, T* dst) {
-        const TileId id = decode_tile(tile, g, TW, cgroups);
+        const TileId id = decode_tile(tile, g, gx.hb0, TW, cgroups);
         const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
         for (int idx = tid; idx < xtotal; idx += NCONS) {
             int c, i, jv;
@@ -608,7 +613,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
 
     // Tile k of this CTA (ring slot k & 3), -1 when the schedule is done.
     auto tile_at = [&](uint32_t k) -> int64_t {
-        if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts, g.wait_budget)) {
+        if (!dead && !mbar_wait(&tile_full[k & 3], (k >> 2) & 1u, timeouts, gx.wait_budget)) {
             dead = true;
             *(volatile int*)&abort_flag = 1;
         }
@@ -617,7 +622,7 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
     int64_t tile = tile_at(0);
     if (tile >= 0) issue_x(tile, xa0);
     for (uint32_t k = 0; tile >= 0; ++k) {
-        const TileId id = decode_tile(tile, g, TW, cgroups);
+        const TileId id = decode_tile(tile, g, gx.hb0, TW, cgroups);
         const int64_t b = id.b;
         const int64_t c0 = (g.Cw == 1) ? 0 : id.grp % cgroups;
         const int h0 = id.h0, w0 = id.w0;
@@ -813,9 +818,9 @@ acc_fast_kernel(const __grid_constant__ WMaps wmaps, const T* __restrict__ x,
                     for (int c = 0; c < NC; ++c) u[c][i] = u[c][i] / sv;
                 }
             }
-            if (bad && invalid && h < g.hb1 && wcol < g.W) atomicOr(invalid, 1);
+            if (bad && invalid && h < gx.hb1 && wcol < g.W) atomicOr(invalid, 1);
         }
-        if (h < g.hb1 && wcol < g.W) {
+        if (h < gx.hb1 && wcol < g.W) {
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const int64_t o = ((b * g.C + c0 + c) * g.H + h) * g.W + wcol;

@@ -16,7 +16,7 @@ namespace fast {
 
 template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT, int MODE>
 bool launch(const WMaps& maps, const void* x, void* U, void* Z,
-            const FastTable& tab, Geo g, unsigned int* timeouts,
+            const FastTable& tab, Geo g, GeoExt gx, unsigned int* timeouts,
             int* invalid, cudaStream_t stream) {
     unsigned long long* ticket = tile_ticket(stream);
     if (!ticket) {
@@ -57,12 +57,12 @@ bool launch(const WMaps& maps, const void* x, void* U, void* Z,
     }
     const int64_t nsm = fast_sm_count();
     int64_t grid_cap = nsm;
-    if (g.max_ctas > 0 && g.max_ctas < grid_cap) grid_cap = g.max_ctas;
+    if (gx.max_ctas > 0 && gx.max_ctas < grid_cap) grid_cap = gx.max_ctas;
     const unsigned grid = static_cast<unsigned>(g.ntiles < grid_cap ? g.ntiles : grid_cap);
     k<<<grid, NTHREADS, smem, stream>>>(maps, static_cast<const T*>(x),
                                         static_cast<float*>(U),
                                         static_cast<float*>(Z), tab, g, timeouts, ticket,
-                                        invalid);
+                                        invalid, gx);
     return true;
 }
 
@@ -71,7 +71,7 @@ bool launch(const WMaps& maps, const void* x, void* U, void* Z,
 
 #define NSC_FAST_ONE(T, NC, A, B, E, M)                                            \
     template bool nsc::fast::launch<T, NC, A, B, E, M>(const WMaps&,                 \
-        const void*, void*, void*, const FastTable&, Geo,                            \
+        const void*, void*, void*, const FastTable&, Geo, GeoExt,                           \
         unsigned int*, int*, cudaStream_t);
 // Every table bucket of one storage type, image-channel count and mode
 // (0: accumulate_uz, 1: normalized log weights, 2: normalized positive).
