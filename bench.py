@@ -706,7 +706,59 @@ def _wl_accumulate_train():
         "f16 in, f32 accumulate", make, cpu)
 
 
-WORKLOADS = {"pair_gather": _wl_pair_gather, "accumulate_train": _wl_accumulate_train, "normalized": _wl_normalized,
+def _wl_normalized_train():
+    """configs[2] forward + backward: normalized_accumulate_uz with logits
+    that require grad, grad_D N(0, 1)."""
+    base = _wl_normalized()
+    Bt, Cx, Hs, Ws, Rr = 16, 3, 512, 512, 7
+    rows = [(dx, dy, 0) for dx in range(-Rr, Rr + 1) for dy in range(-Rr, Rr + 1)]
+    Sn = len(rows)
+
+    def make(dev, b0, nb):
+        import neural_shift_cuda_b200 as nsc
+        w = base.make(dev, b0, nb)
+        x, lg = w["inputs"]
+        gD = _seeded((Cx, Hs, Ws), b0, nb, 8, dev,
+                     lambda g, sh: torch.randn(sh, generator=g, device=dev))
+        sh = torch.tensor(rows)
+
+        def run(a, b, gd):
+            b = b.detach().requires_grad_(True)
+            a = a.detach().requires_grad_(True)
+            # the channel-broadcast (S*B, 1, H, W) form: an expand + slice of the
+            # logits would add the autograd scatter/sum of a 3-channel gradient
+            D, L = nsc.normalized_accumulate_uz(a, b, sh, log_weights=True,
+                                                return_log_degree=True, validate=False)
+            gx, gl = torch.autograd.grad(D, (a, b), gd)
+            return D.detach(), gx, gl
+        return dict(inputs=[x, lg, gD], run=run, launches=2,
+                    units=2 * Sn * nb * Cx * Hs * Ws)
+
+    def cpu(nb):
+        from oracle import nsc_oracle as O
+        g = torch.Generator().manual_seed(0)
+        rows_s = 32
+        x = torch.rand(1, Cx, rows_s, Ws, generator=g).to(torch.bfloat16)
+        lg = (3.0 * torch.randn(Sn, 1, rows_s, Ws, generator=g)).to(torch.bfloat16)
+        gD = torch.randn(1, Cx, rows_s, Ws, generator=g)
+        t0 = time.perf_counter()
+        D, L = O.normalized_accumulate_uz(x, lg.expand(-1, Cx, -1, -1), torch.tensor(rows), True)
+        O.normalized_accumulate_uz_backward(x, lg, D, L, gD, torch.zeros_like(gD),
+                                            torch.tensor(rows), True)
+        return (2 * Sn * Cx * rows_s * Ws, time.perf_counter() - t0,
+                f"oracle normalized_accumulate_uz fwd+bwd (log) on a (1,3,{rows_s},512) band, S={Sn}")
+
+    return OpWorkload(
+        "normalized_train", "pixel-shifts/s (normalized_accumulate_uz fwd+bwd, log weights, "
+        "GASD configs[2]: x bf16 (16,3,512,512), S=225)", Bt,
+        {"workload": "normalized_accumulate_uz forward + backward, logits N(0,9) bf16 "
+                     "channel-shared, full window R=7 S=225, x bf16 (16,3,512,512), "
+                     "grad_D N(0,1) (configs[2])"},
+        "bf16 in, f32 accumulate", make, cpu)
+
+
+WORKLOADS = {"pair_gather": _wl_pair_gather, "accumulate_train": _wl_accumulate_train,
+             "normalized_train": _wl_normalized_train, "normalized": _wl_normalized,
              "metropolis": _wl_metropolis,
              "nectr": lambda: _wl_nectr("f32"),
              "nectr_bf16": lambda: _wl_nectr("bf16"),
