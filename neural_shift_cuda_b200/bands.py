@@ -278,7 +278,8 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
                          compute: Optional[Callable] = None, *, padded: bool = False,
                          forward: Callable = band_forward_cuda,
                          edges: Callable = band_edges_cuda,
-                         overlap: bool = True, deadline: Optional[float] = None):
+                         overlap: Optional[bool] = None,
+                         deadline: Optional[float] = None):
     """accumulate_uz of this rank's band of a row-split image.
 
     x_band: (B, C, Hb, W) this rank's rows of x -- or, with padded=True,
@@ -291,7 +292,11 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
     (U, Z, top, bot) (run after the halo arrives).  overlap=True (CUDA
     forward only): the x halo travels during the edge-strip kernel and the
     strips during the band forward, which runs on all but
-    NSC_BAND_RESERVE_SMS (default 2) SMs.  deadline (seconds): an exchange
+    NSC_BAND_RESERVE_SMS (default 2) SMs.  It measured no faster than one
+    grouped exchange on 2 and 4 B200s at configs[4] (4.69 vs 4.67 ms and
+    2.53 vs 2.51 ms per step: the exchange is short and the reserved SMs cost
+    the forward about what they hide), so overlap=None takes it from
+    NSC_BAND_OVERLAP=1 and defaults to off.  deadline (seconds): an exchange
     that has not completed in time, or whose peer left, raises
     BandExchangeError (the process group's own timeout applies otherwise)."""
     import torch.distributed as dist
@@ -314,8 +319,9 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
             return compute(xe, wb, sh, r0, hg)[2:]
         def forward(xe, wb, sh, r0, hg):        # noqa: F811
             return compute(xe, wb, sh, r0, hg)[:2]
-    import os
-    overlap = overlap and os.environ.get("NSC_BAND_OVERLAP", "1") != "0"
+    if overlap is None:
+        import os
+        overlap = os.environ.get("NSC_BAND_OVERLAP", "0") == "1"
     if (overlap and compute is None and forward is band_forward_cuda
             and x_pad.is_cuda):
         # x halo in flight during the edge-strip kernel; the strips in flight
