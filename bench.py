@@ -336,7 +336,7 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
-                        "max": max(step_ms)},
+                        "max": max(step_ms), "slowest": step_ms.index(max(step_ms))},
             "clocks": clocks,
             "self_check": {"finite_and_nonnegative_Z": ok},
         }

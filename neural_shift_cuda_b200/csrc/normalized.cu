@@ -354,6 +354,173 @@ norm_bwd_gw_bcast_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
     }
 }
 
+// Tiled backward (the same gradients as norm_bwd_kernel), for fp16 / bf16 /
+// fp32 storage and radius <= 8.  A CTA of 32 x 8 threads owns a 16 x 32
+// tile of one (image, weight channel) group, two pixels per thread (rows 8
+// apart).  x, D, grad_D, grad_log_C of the group's channels and log_C are
+// staged once, circularly, with the R halo as fp32 in shared memory; every
+// neighbour read of the shift loop is a shared-memory load at a constant
+// offset, and the mirror term's inside test is a flag (interior tiles
+// skip it).  log_C is the same for every channel of a channel-broadcast
+// weight (the keys are shared), so it is staged and exponentiated once.
+// exp(lw - lc) (0 where either is -inf) through ex2.approx: a few ulp of
+// fp32, well inside the fp32 tolerance of the gradients.
+__device__ __forceinline__ float ex2_fast(float v) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+__device__ __forceinline__ float fraction_fast(float lw, float lc) {
+    if (lw == -INFINITY || lc == -INFINITY) return 0.f;
+    return ex2_fast((lw - lc) * 1.4426950408889634f);
+}
+
+constexpr int kTX = 32, kTY = 8, kPPT = 2, kTH = kTY * kPPT, kTW = kTX;
+
+template <typename T, int NC>
+__global__ void __launch_bounds__(kTX * kTY)
+norm_bwd_tile_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                     const float* __restrict__ D, const float* __restrict__ L,
+                     const float* __restrict__ gD, const float* __restrict__ gL,
+                     float* __restrict__ gx, T* __restrict__ gw, const ShiftTable st,
+                     int B, int C, int H, int W, int Cw, int R, int tiles_x, int logw) {
+    extern __shared__ __align__(16) float smem_n[];
+    const int XP = kTW + 2 * R, XR = kTH + 2 * R, plane = XP * XR;
+    float* sx = smem_n;                 // [NC] x
+    float* sD = sx + NC * plane;        // [NC] D
+    float* sgD = sD + NC * plane;       // [NC] grad_D
+    float* sgL = sgD + NC * plane;      // [NC] grad_log_C
+    float* sL = sgL + NC * plane;       // log_C (shared by the group's channels)
+    const int64_t HW = static_cast<int64_t>(H) * W;
+    const int cgroups = Cw == 1 ? 1 : C;
+    const int grp = blockIdx.y;
+    const int b = grp / cgroups;
+    const int wc = Cw == 1 ? 0 : grp % cgroups;
+    const int c0 = Cw == 1 ? 0 : wc;
+    const int ty = blockIdx.x / tiles_x;
+    const int h0 = ty * kTH, w0 = (blockIdx.x - ty * tiles_x) * kTW;
+    const int64_t cb = (static_cast<int64_t>(b) * C + c0) * HW;
+    const int tid = threadIdx.y * kTX + threadIdx.x;
+    for (int e = tid; e < plane; e += kTX * kTY) {
+        const int i = e / XP, j = e - i * XP;
+        int r = (h0 - R + i) % H;
+        if (r < 0) r += H;
+        int c = (w0 - R + j) % W;
+        if (c < 0) c += W;
+        const int64_t off = static_cast<int64_t>(r) * W + c;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            sx[k * plane + e] = to_acc(x[cb + k * HW + off]);
+            sD[k * plane + e] = D[cb + k * HW + off];
+            sgD[k * plane + e] = gD[cb + k * HW + off];
+            sgL[k * plane + e] = gL[cb + k * HW + off];
+        }
+        sL[e] = L[cb + off];
+    }
+    __syncthreads();
+    const int wcol = w0 + threadIdx.x;
+    if (wcol >= W) return;
+    const bool interior = h0 - R >= 0 && h0 + kTH + R <= H && w0 - R >= 0 && w0 + kTW + R <= W;
+    const T* __restrict__ wb = w + (static_cast<int64_t>(b) * Cw + wc) * HW;
+    T* __restrict__ gwb = gw + (static_cast<int64_t>(b) * Cw + wc) * HW;
+    const int64_t sstride = static_cast<int64_t>(B) * Cw * HW;
+    int hh[kPPT], ci[kPPT];
+    float Lq[kPPT], eLq[kPPT], xq[kPPT][NC], Dq[kPPT][NC], gDq[kPPT][NC], gLq[kPPT][NC];
+    float acc[kPPT][NC];
+#pragma unroll
+    for (int p = 0; p < kPPT; ++p) {
+        const int h = h0 + threadIdx.y + kTY * p;
+        hh[p] = h < H ? h : H - 1;
+        ci[p] = (threadIdx.y + kTY * p + R) * XP + threadIdx.x + R;
+        Lq[p] = sL[ci[p]];
+        eLq[p] = exp_acc(-Lq[p]);   // positive mode: exp(-log_C), once per pixel
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            xq[p][k] = sx[k * plane + ci[p]];
+            Dq[p][k] = sD[k * plane + ci[p]];
+            gDq[p][k] = sgD[k * plane + ci[p]];
+            gLq[p][k] = sgL[k * plane + ci[p]];
+            acc[p][k] = 0.f;
+        }
+    }
+    // Weights of the next LA shifts are loaded ahead of their use (a small
+    // register ring), so each thread keeps 2 * kPPT * LA loads in flight.
+    constexpr int LA = 6;
+    float wq_r[LA][kPPT], ws_r[LA][kPPT];
+    auto fetch = [&](int s, float (&wq)[kPPT], float (&wsrc)[kPPT]) {
+        const int dx = st.dx[s], dy = st.dy[s];
+        const T* ws = wb + s * sstride;
+#pragma unroll
+        for (int p = 0; p < kPPT; ++p) {
+            const int h = hh[p];
+            const int64_t q = static_cast<int64_t>(h) * W + wcol;
+            const int64_t qsrc = static_cast<int64_t>(wrap1(h - dx, H)) * W + wrap1(wcol - dy, W);
+            wq[p] = to_acc(__ldg(ws + q));
+            wsrc[p] = to_acc(__ldg(ws + qsrc));
+        }
+    };
+#pragma unroll
+    for (int k = 0; k < LA; ++k)
+        if (k < st.S) fetch(k, wq_r[k], ws_r[k]);
+    for (int s0 = 0; s0 < st.S; s0 += LA) {
+#pragma unroll
+        for (int k = 0; k < LA; ++k) {
+            const int s = s0 + k;
+            if (s >= st.S) break;
+            float wqv[kPPT], wsv[kPPT];
+#pragma unroll
+            for (int p = 0; p < kPPT; ++p) {
+                wqv[p] = wq_r[k][p];
+                wsv[p] = ws_r[k][p];
+            }
+            if (s + LA < st.S) fetch(s + LA, wq_r[k], ws_r[k]);
+            const int dx = st.dx[s], dy = st.dy[s];
+            const bool inv = st.has_inv(s), per = st.has_per(s);
+            const int off = dx * XP + dy;
+#pragma unroll
+            for (int p = 0; p < kPPT; ++p) {
+                const int h = hh[p];
+                const int64_t q = static_cast<int64_t>(h) * W + wcol;
+                const bool in_f = interior || (inb(h + dx, H) && inb(wcol + dy, W));
+                const float lw_src = as_log(wsv[p], logw);
+                const float lw_q = as_log(wqv[p], logw);
+                const int qs = ci[p] - off, qf = ci[p] + off;
+                const float pa = fraction_fast(lw_src, sL[qs]);
+                const float fq = logw ? fraction_fast(lw_q, Lq[p]) : eLq[p];
+                const bool mir = inv && (per || in_f);
+                float pb = 0.f, fm = 0.f;
+                if (mir) {
+                    const float Lf = sL[qf];
+                    pb = fraction_fast(lw_q, Lf);
+                    fm = logw ? pb : ex2_fast(-Lf * 1.4426950408889634f);
+                }
+                float gws = 0.f;
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    acc[p][c] += pa * sgD[c * plane + qs];
+                    gws += fq * (gDq[p][c] * (sx[c * plane + qf] - Dq[p][c]) + gLq[p][c]);
+                    if (mir) {
+                        const float gDi = sgD[c * plane + qf];
+                        acc[p][c] += pb * gDi;
+                        gws += fm * (gDi * (xq[p][c] - sD[c * plane + qf]) + sgL[c * plane + qf]);
+                    }
+                }
+                if (lw_q == neg_inf<float>()) gws = 0.f;
+                if (h0 + static_cast<int>(threadIdx.y) + kTY * p < H)
+                    gwb[s * sstride + q] = static_cast<T>(gws);
+            }
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < kPPT; ++p) {
+        const int h = h0 + threadIdx.y + kTY * p;
+        if (h >= H) continue;
+#pragma unroll
+        for (int k = 0; k < NC; ++k)
+            gx[cb + k * HW + static_cast<int64_t>(h) * W + wcol] = acc[p][k];
+    }
+}
+
 template <int NC> struct NCTag { static constexpr int value_nc = NC; };
 
 template <typename F>
@@ -493,6 +660,49 @@ nsc_status nsc_normalized_accumulate_uz_bwd(
     if (!x || !w || !D || !log_C || !grad_D || !grad_log_C || !grad_x || !grad_w)
         return fail(NSC_ERR_INVALID_ARG, "%s: NULL tensor pointer", op);
     cudaStream_t sm = as_stream(stream);
+    // tiled form: storage fp16 / bf16 / fp32 shared by x and w, radius <= 8
+    const int64_t ngrp = B * (w_channels == 1 ? 1 : C);
+    if (!getenv("NSC_NORM_GENERIC") && x_dtype == w_dtype && x_dtype != NSC_F64 &&
+        (w_channels == C || (w_channels == 1 && (C == 1 || C == 3))) && st.R <= 8 &&
+        ngrp <= 65535 && H < (1LL << 30) && W < (1LL << 30) && B * C < (1LL << 30)) {
+        const int R = st.R;
+        const int tiles_x = static_cast<int>((W + kTW - 1) / kTW);
+        const int64_t tiles = tiles_x * ((H + kTH - 1) / kTH);
+        const int NC = w_channels == 1 ? static_cast<int>(C) : 1;
+        const size_t smem = static_cast<size_t>(4 * NC + 1) * (kTW + 2 * R) * (kTH + 2 * R) *
+                            sizeof(float);
+        if (tiles < (1LL << 31)) {
+            auto go = [&](auto kern, auto tptr) {
+                using T = std::remove_const_t<std::remove_pointer_t<decltype(tptr)>>;
+                if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)) != cudaSuccess) {
+                    cudaGetLastError();
+                    return false;
+                }
+                kern<<<dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(ngrp)),
+                       dim3(kTX, kTY), smem, sm>>>(
+                    static_cast<const T*>(x), static_cast<const T*>(w),
+                    static_cast<const float*>(D), static_cast<const float*>(log_C),
+                    static_cast<const float*>(grad_D), static_cast<const float*>(grad_log_C),
+                    static_cast<float*>(grad_x), static_cast<T*>(grad_w), st,
+                    static_cast<int>(B), static_cast<int>(C), static_cast<int>(H),
+                    static_cast<int>(W), static_cast<int>(w_channels), R, tiles_x,
+                    log_weights ? 1 : 0);
+                return true;
+            };
+            bool ran;
+            if (x_dtype == NSC_F16)
+                ran = NC == 3 ? go(norm_bwd_tile_kernel<__half, 3>, (const __half*)nullptr)
+                              : go(norm_bwd_tile_kernel<__half, 1>, (const __half*)nullptr);
+            else if (x_dtype == NSC_BF16)
+                ran = NC == 3 ? go(norm_bwd_tile_kernel<__nv_bfloat16, 3>, (const __nv_bfloat16*)nullptr)
+                              : go(norm_bwd_tile_kernel<__nv_bfloat16, 1>, (const __nv_bfloat16*)nullptr);
+            else
+                ran = NC == 3 ? go(norm_bwd_tile_kernel<float, 3>, (const float*)nullptr)
+                              : go(norm_bwd_tile_kernel<float, 1>, (const float*)nullptr);
+            if (ran) return check_launch(op);
+        }
+    }
     return with_types(op, x_dtype, w_dtype, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;

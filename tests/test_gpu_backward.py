@@ -62,3 +62,47 @@ def test_tiled_grad_w_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, tabl
     torch.testing.assert_close(gw.float(), gw2.float(),
                                rtol=1e-4 if dtype == torch.float32 else 1e-2,
                                atol=1e-4 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("dtype,C,Cw,H,W,table,logw,periodic", [
+    (torch.float32, 3, 1, 40, 64, ("window", 7), True, False),    # GASD family
+    (torch.float32, 1, 1, 30, 48, ("half", 5), True, False),      # NECTR family
+    (torch.float32, 3, 1, 23, 37, ("half", 3), False, False),     # positive, odd sizes
+    (torch.float32, 2, 2, 17, 33, ("half", 2), False, True),      # per-channel, periodic
+    (torch.bfloat16, 3, 1, 19, 40, ("window", 4), True, False),
+    (torch.float16, 1, 1, 9, 12, ("half", 8), True, False),       # image smaller than halo
+])
+def test_tiled_normalized_backward_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W,
+                                                  table, logw, periodic):
+    """The tiled normalized backward (csrc/normalized.cu, norm_bwd_tile_kernel)
+    against the oracle's analytic gradients and the general kernel."""
+    torch.manual_seed(H * W + C)
+    kind, R = table
+    rows = O.halfplane_shifts(R) if kind == "half" else O.window_shifts(R)
+    sh = torch.tensor(rows)
+    S, B = len(rows), 2
+    x = torch.rand(B, C, H, W).to(dtype)
+    raw = torch.randn(S * B, Cw, H, W)
+    k = (2.0 * raw if logw else raw.exp()).to(dtype)
+    gD, gL = torch.randn(B, C, H, W), torch.randn(B, C, H, W)
+
+    def grads():
+        xc = x.to(cuda).requires_grad_(True)
+        kc = k.to(cuda).requires_grad_(True)
+        D, L = nsc.normalized_accumulate_uz(xc, kc, sh, log_weights=logw,
+                                            return_log_degree=True, validate=False,
+                                            periodic_mirror=periodic)
+        return [t.cpu() for t in torch.autograd.grad((D, L), (xc, kc),
+                                                     (gD.to(cuda), gL.to(cuda)))]
+    gx, gk = grads()
+    rows_o = [(dx, dy, 2 if (inv and periodic) else int(inv)) for dx, dy, inv in rows]
+    kk = k.expand(-1, C, -1, -1) if Cw == 1 else k
+    Dr, Lr = O.normalized_accumulate_uz(x, kk, rows_o, logw)
+    gxr, gkr = O.normalized_accumulate_uz_backward(x, k, Dr, Lr, gD, gL, rows_o, logw)
+    tol = 2e-4 if dtype == torch.float32 else 2e-2
+    torch.testing.assert_close(gx.float(), gxr.to(dtype).float(), rtol=tol, atol=tol)
+    torch.testing.assert_close(gk.float(), gkr.to(dtype).float(), rtol=tol, atol=tol)
+    monkeypatch.setenv("NSC_NORM_GENERIC", "1")
+    gx2, gk2 = grads()
+    torch.testing.assert_close(gx.float(), gx2.float(), rtol=tol, atol=tol)
+    torch.testing.assert_close(gk.float(), gk2.float(), rtol=tol, atol=tol)
