@@ -241,6 +241,49 @@ acc_per_fix_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
     }
 }
 
+// After the tiled grad_x (accumulate_gx_tma.cuh): gx += the wrapped part of
+// term A, sum_s [q - d outside] w_s((q - d) mod) gU((q - d) mod), for the
+// pixels within R of the image border (one thread per pixel; the tile
+// kernel counted q - d inside).
+template <typename TW, int NC>
+__global__ void __launch_bounds__(256)
+acc_gx_wrap_kernel(const float* __restrict__ gU, const TW* __restrict__ w,
+                   float* __restrict__ gx, const ShiftTable st, int64_t B, int64_t C,
+                   int64_t H, int64_t W, int64_t Cw, int64_t R, int64_t nb, int64_t groups) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (i >= nb) return;
+    int64_t h, wcol;
+    border_pixel(i, H, W, R, h, wcol);
+    const int64_t plane = H * W;
+    const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
+    for (int64_t g = blockIdx.y; g < groups; g += gridDim.y) {
+        const int64_t b = g / cgroups;
+        const int64_t cg = g % cgroups;
+        const int64_t c0 = (Cw == 1) ? cg * NC : cg;
+        const int64_t wc = (Cw == 1) ? 0 : cg;
+        const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
+        const float* gb = gU + (b * C + c0) * plane;
+        float u[NC];
+#pragma unroll
+        for (int k = 0; k < NC; ++k) u[k] = 0.f;
+        for (int s = 0; s < st.S; ++s) {
+            int64_t hm = h - st.dx[s], wm = wcol - st.dy[s];
+            if (inb(hm, H) && inb(wm, W)) continue;     // counted by the tile kernel
+            hm = wrap1(hm, H);
+            wm = wrap1(wm, W);
+            const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane;
+            const float mv = ldg_acc<TW, float>(ws + hm * W + wm);
+#pragma unroll
+            for (int k = 0; k < NC; ++k)
+                if (k < nc) u[k] += mv * gb[k * plane + hm * W + wm];
+        }
+        const int64_t ob = (b * C + c0) * plane + h * W + wcol;
+#pragma unroll
+        for (int k = 0; k < NC; ++k)
+            if (k < nc) gx[ob + k * plane] += u[k];
+    }
+}
+
 // U/Z += neighbour strips; one thread per strip element and strip.
 template <typename A>
 __global__ void __launch_bounds__(256)
@@ -477,6 +520,27 @@ nsc_status acc_per_fix(const void* x, int xd, const void* w, int wd, int64_t Cw,
     });
 }
 
+nsc_status acc_gx_wrap(const void* w, int wd, int64_t Cw, int64_t B, int64_t C,
+                       int64_t H, int64_t W, const ShiftTable& st, const void* gU,
+                       void* gx, cudaStream_t stream) {
+    const int64_t R = st.R;
+    const int64_t nb = border_count(H, W, R);
+    if (nb == 0) return ok();
+    return with_types("accumulate_uz_backward", NSC_F32, wd, [&](auto, auto tw) {
+        using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
+        with_nc(C, Cw, [&](auto tag) {
+            constexpr int NC = decltype(tag)::value_nc;
+            const int64_t groups = n_groups(B, C, Cw, NC);
+            const dim3 grid(grid_1d(nb, 256),
+                            static_cast<unsigned>(groups < 65535 ? groups : 65535));
+            acc_gx_wrap_kernel<TW, NC><<<grid, 256, 0, stream>>>(
+                static_cast<const float*>(gU), static_cast<const TW*>(w),
+                static_cast<float*>(gx), st, B, C, H, W, Cw, R, nb, groups);
+        });
+        return check_launch("accumulate_uz_backward");
+    });
+}
+
 nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
                      int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t row0,
                      int64_t Hg, const ShiftTable& st, void* top, void* bot,
@@ -531,6 +595,11 @@ nsc_status acc_bwd(const void* x, int xd, const void* w, int wd, int64_t Cw,
     const bool gw_done = acc_gw_fast(x, xd, wd, Cw, B, C, H, W, st, gU, gZ, gw, stream);
     if (gw_done && acc_gx_fast(w, xd, wd, Cw, B, C, H, W, st, gU, gx, stream))
         return check_launch("accumulate_uz_backward");
+    if (std::getenv("NSC_REQUIRE_FAST"))
+        return fail(NSC_ERR_INVALID_ARG,
+                    "accumulate_uz_backward: a tiled kernel declined this call "
+                    "(NSC_REQUIRE_FAST is set): %s", gw_done ? fast_decline_reason()
+                                                             : "grad_w");
     return with_types("accumulate_uz_backward", xd, wd, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;

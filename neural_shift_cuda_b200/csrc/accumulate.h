@@ -41,6 +41,16 @@ bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C
                  int64_t H, int64_t W, const ShiftTable& st, const void* gU, void* gx,
                  cudaStream_t stream);
 
+// Tiled TMA grad_x (accumulate_gx_tma.cuh) followed by its border-band
+// wrap kernel: weights fp16 / bf16 / fp32, grad_U and grad_x fp32.  false
+// (nothing launched) when it declines.
+bool acc_gx_tma(const void* w, int wd, int64_t Cw, int64_t B, int64_t C, int64_t H,
+                int64_t W, const ShiftTable& st, const void* gU, void* gx,
+                cudaStream_t stream);
+nsc_status acc_gx_wrap(const void* w, int wd, int64_t Cw, int64_t B, int64_t C,
+                       int64_t H, int64_t W, const ShiftTable& st, const void* gU,
+                       void* gx, cudaStream_t stream);
+
 // After a tiled forward (mode 0) of a table with periodic mirror rows: add
 // the wrapped mirror terms the tile kernel leaves out (border band only).
 nsc_status acc_per_fix(const void* x, int xd, const void* w, int wd, int64_t Cw,

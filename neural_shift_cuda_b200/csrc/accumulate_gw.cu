@@ -483,6 +483,12 @@ bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C
                  int64_t H, int64_t W, const ShiftTable& st, const void* gU, void* gx,
                  cudaStream_t stream) {
     using namespace gwk;
+    // the TMA kernel first; NSC_GX_LEGACY selects the kernel below, and
+    // NSC_REQUIRE_FAST (a test switch) makes a decline of the TMA kernel fail
+    if (!std::getenv("NSC_GX_LEGACY")) {
+        if (acc_gx_tma(w, wd, Cw, B, C, H, W, st, gU, gx, stream)) return true;
+        if (std::getenv("NSC_REQUIRE_FAST")) return false;
+    }
     GwTable tab;
     GwGeo g;
     int lo, hi;

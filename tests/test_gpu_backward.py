@@ -106,3 +106,41 @@ def test_tiled_normalized_backward_matches_oracle(cuda, monkeypatch, dtype, C, C
     gx2, gk2 = grads()
     torch.testing.assert_close(gx.float(), gx2.float(), rtol=tol, atol=tol)
     torch.testing.assert_close(gk.float(), gk2.float(), rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype,C,Cw,H,W,table", [
+    (torch.bfloat16, 3, 1, 70, 256, ("half", 10)),    # configs[4] family
+    (torch.float16, 3, 1, 45, 136, ("half", 5)),      # partial tiles
+    (torch.float32, 3, 1, 33, 72, ("half", 10)),      # fp32 weights, W % 64 != 0
+    (torch.float32, 1, 1, 61, 128, ("window", 6)),    # negative dy
+    (torch.bfloat16, 2, 2, 31, 80, ("window", 4)),    # per-channel weights
+    (torch.float16, 1, 1, 25, 32, ("half", 12)),      # image narrower than a tile
+    (torch.float32, 3, 1, 13, 16, ("half", 2)),
+])
+def test_tma_grad_x_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, table):
+    """The TMA grad_x kernel (csrc/accumulate_gx_tma.cuh + the border-band
+    wrap kernel) must take these calls (NSC_REQUIRE_FAST makes a decline an
+    error) and match the oracle and the earlier tiled kernel (NSC_GX_LEGACY).
+    grad_x is computed in fp32 and returned in x's dtype: fp32 within 1e-4,
+    fp16 / bf16 within one rounding of the fp32 oracle."""
+    torch.manual_seed(3 * H + W)
+    kind, R = table
+    rows = O.halfplane_shifts(R) if kind == "half" else O.window_shifts(R)
+    sh = torch.tensor(rows)
+    S = len(rows)
+    B = 2
+    x = torch.rand(B, C, H, W).to(dtype)
+    w = torch.rand(S * B, Cw, H, W).to(dtype)
+    gU, gZ = torch.randn(B, C, H, W), torch.randn(B, C, H, W)
+    monkeypatch.setenv("NSC_REQUIRE_FAST", "1")
+    gx, _ = _grads(x, w, sh, gU, gZ, cuda)
+    monkeypatch.delenv("NSC_REQUIRE_FAST")
+    gxr, _ = O.accumulate_uz_backward(x, w, gU, gZ, sh)
+    if dtype == torch.float32:
+        torch.testing.assert_close(gx, gxr, rtol=1e-4, atol=1e-4)
+    else:
+        torch.testing.assert_close(gx.float(), gxr.to(dtype).float(), rtol=1e-2, atol=1e-2)
+    monkeypatch.setenv("NSC_GX_LEGACY", "1")
+    gx2, _ = _grads(x, w, sh, gU, gZ, cuda)
+    tol = 1e-4 if dtype == torch.float32 else 1e-2
+    torch.testing.assert_close(gx.float(), gx2.float(), rtol=tol, atol=tol)
