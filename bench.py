@@ -679,7 +679,8 @@ def _wl_accumulate_train():
             U, Z = nsc.accumulate_uz(xi, wi, sh)
             gx, gw = torch.autograd.grad((U, Z), (xi, wi), (a, b))
             return U.detach(), Z.detach(), gx, gw
-        return dict(inputs=[x, w, gU, gZ], run=run, launches=2,
+        # forward, grad_w, grad_x (TMA tile kernel + border-band wrap kernel)
+        return dict(inputs=[x, w, gU, gZ], run=run, launches=4,
                     units=2 * S * C * Hs * Ws)
 
     def cpu(nb):

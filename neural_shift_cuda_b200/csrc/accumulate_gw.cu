@@ -93,7 +93,12 @@ __device__ __forceinline__ void load_row(float (&d)[N], const float* p) {
     }
 }
 
-template <typename T, int NC, int DYMIN, int DYMAX>
+// EXACT: the table is the canonical half-plane table of radius R = tab.Rx
+// <= DYMAX (every dx in [-R, R] with dy = 1..R, all with mirror terms, plus
+// (dx, 0) for dx >= 0 with a mirror term for dx > 0), so whether an entry
+// exists and has a mirror term is a uniform test of the compile-time dy
+// against R (or of dx for dy = 0) instead of per-entry bit tests.
+template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
 __global__ void __launch_bounds__(NT)
 acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
               const float* __restrict__ gZ, T* __restrict__ gw, const GwTable tab,
@@ -159,6 +164,17 @@ acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
         const uint32_t pres = static_cast<uint32_t>(tab.present[dx + MAXR] >> (DYMIN + MAXR));
         if (!pres) continue;
         const uint32_t invm = static_cast<uint32_t>(tab.inv[dx + MAXR] >> (DYMIN + MAXR));
+        // entry j (dy = DYMIN + j) present / with a mirror term
+        auto has = [&](auto jc) -> bool {
+            constexpr int j = decltype(jc)::value;
+            if constexpr (EXACT) return j > 0 ? j <= Rx : dx >= 0;
+            else return (pres >> j) & 1u;
+        };
+        auto mir = [&](auto jc) -> bool {
+            constexpr int j = decltype(jc)::value;
+            if constexpr (EXACT) return j > 0 ? j <= Rx : dx > 0;
+            else return (invm >> j) & 1u;
+        };
         float acc[NDY][V];
 #pragma unroll
         for (int j = 0; j < NDY; ++j)
@@ -174,8 +190,8 @@ acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
             load_row<V, true>(go, sg + c * plane + own);
             sfor<0, NDY>([&](auto jc) {
                 constexpr int j = decltype(jc)::value;
-                if (!((pres >> j) & 1u)) return;
-                if ((invm >> j) & 1u) {
+                if (!has(jc)) return;
+                if (mir(jc)) {
 #pragma unroll
                     for (int i = 0; i < V; ++i)
                         acc[j][i] = fmaf(xo[i], gwn[j + i], fmaf(go[i], xw[j + i], acc[j][i]));
@@ -189,8 +205,8 @@ acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
         load_row<NWIN, DYMIN % 4 == 0>(zw, sz + wrow);
         sfor<0, NDY>([&](auto jc) {
             constexpr int j = decltype(jc)::value;
-            if (!((pres >> j) & 1u)) return;
-            const bool iv = (invm >> j) & 1u;
+            if (!has(jc)) return;
+            const bool iv = mir(jc);
             float v[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) v[i] = acc[j][i] + zo[i] + (iv ? zw[j + i] : 0.f);
@@ -338,10 +354,10 @@ acc_gx_kernel(const T* __restrict__ w, const float* __restrict__ gU,
     }
 }
 
-template <typename T, int NC, int LO, int HI>
+template <typename T, int NC, int LO, int HI, bool EXACT>
 bool launch(const void* x, const void* gU, const void* gZ, void* gw, const GwTable& tab,
             const GwGeo& g, size_t smem, dim3 grid, cudaStream_t stream) {
-    auto k = acc_gw_kernel<T, NC, LO, HI>;
+    auto k = acc_gw_kernel<T, NC, LO, HI, EXACT>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess) {
         cudaGetLastError();
@@ -353,14 +369,18 @@ bool launch(const void* x, const void* gU, const void* gZ, void* gw, const GwTab
 }
 
 template <typename T, int NC>
-bool by_range(int lo, int hi, const void* x, const void* gU, const void* gZ, void* gw,
-              const GwTable& tab, const GwGeo& g, size_t smem, dim3 grid,
+bool by_range(bool exact, int lo, int hi, const void* x, const void* gU, const void* gZ,
+              void* gw, const GwTable& tab, const GwGeo& g, size_t smem, dim3 grid,
               cudaStream_t st) {
-#define NSC_GW(L, H) \
-    if (lo == L && hi == H) return launch<T, NC, L, H>(x, gU, gZ, gw, tab, g, smem, grid, st);
+#define NSC_GW(L, H)                                                                    \
+    if (lo == L && hi == H)                                                           \
+        return exact ? launch<T, NC, L, H, true>(x, gU, gZ, gw, tab, g, smem, grid, st) \
+                     : launch<T, NC, L, H, false>(x, gU, gZ, gw, tab, g, smem, grid, st);
     NSC_GW(0, 2) NSC_GW(0, 4) NSC_GW(0, 6) NSC_GW(0, 8) NSC_GW(0, 10) NSC_GW(0, 12)
-    NSC_GW(-4, 4) NSC_GW(-6, 6)
 #undef NSC_GW
+    // tables reaching negative dy are never canonical half-plane tables
+    if (lo == -4 && hi == 4) return launch<T, NC, -4, 4, false>(x, gU, gZ, gw, tab, g, smem, grid, st);
+    if (lo == -6 && hi == 6) return launch<T, NC, -6, 6, false>(x, gU, gZ, gw, tab, g, smem, grid, st);
     return false;
 }
 
@@ -390,17 +410,17 @@ bool gx_by_range(int lo, int hi, const void* w, const void* gU, void* gx,
     return false;
 }
 
-inline bool dispatch(int xd, int NC, int lo, int hi, const void* x, const void* gU,
-                     const void* gZ, void* gw, const GwTable& tab, const GwGeo& g,
-                     size_t smem, dim3 grid, cudaStream_t st) {
+inline bool dispatch(int xd, int NC, bool exact, int lo, int hi, const void* x,
+                     const void* gU, const void* gZ, void* gw, const GwTable& tab,
+                     const GwGeo& g, size_t smem, dim3 grid, cudaStream_t st) {
     if (xd == NSC_F16)
-        return NC == 3 ? by_range<__half, 3>(lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st)
-                       : by_range<__half, 1>(lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st);
+        return NC == 3 ? by_range<__half, 3>(exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st)
+                       : by_range<__half, 1>(exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st);
     if (xd == NSC_BF16)
-        return NC == 3 ? by_range<__nv_bfloat16, 3>(lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st)
-                       : by_range<__nv_bfloat16, 1>(lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st);
-    return NC == 3 ? by_range<float, 3>(lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st)
-                   : by_range<float, 1>(lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st);
+        return NC == 3 ? by_range<__nv_bfloat16, 3>(exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st)
+                       : by_range<__nv_bfloat16, 1>(exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st);
+    return NC == 3 ? by_range<float, 3>(exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st)
+                   : by_range<float, 1>(exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, st);
 }
 
 }  // namespace gwk
@@ -476,7 +496,21 @@ bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C
     if (smem > 227u * 1024u) return false;
     const dim3 grid(static_cast<unsigned>(g.tiles_x * g.tiles_y),
                     static_cast<unsigned>(B * (Cw == 1 ? 1 : C)));
-    return gwk::dispatch(xd, NC, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, stream);
+    // canonical half-plane table of radius R = tab.Rx <= hi (acc_gw_kernel's
+    // EXACT): every present / mirror bit as the pattern says, nothing else
+    const int R = tab.Rx;
+    bool exact = lo == 0 && R >= 1 && R <= hi;
+    for (int dx = -R; exact && dx <= R; ++dx) {
+        uint64_t pres = 0, mir = 0;
+        for (int dy = 0; dy <= R; ++dy) {
+            const uint64_t bit = 1ull << (dy + MAXR);
+            if (dy > 0 || dx >= 0) pres |= bit;
+            if (dy > 0 || dx > 0) mir |= bit;
+        }
+        exact = tab.present[dx + MAXR] == pres && tab.inv[dx + MAXR] == mir;
+    }
+    if (std::getenv("NSC_GW_GENERIC")) exact = false;
+    return gwk::dispatch(xd, NC, exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, stream);
 }
 
 bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C,

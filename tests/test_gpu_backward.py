@@ -64,6 +64,26 @@ def test_tiled_grad_w_matches_oracle(cuda, monkeypatch, dtype, C, Cw, H, W, tabl
                                atol=1e-4 if dtype == torch.float32 else 1e-2)
 
 
+@pytest.mark.parametrize("dtype,C,H,W,R", [
+    (torch.float16, 3, 40, 256, 10),
+    (torch.float32, 3, 23, 132, 3),
+    (torch.bfloat16, 1, 17, 64, 5),
+])
+def test_grad_w_half_plane_pattern_equals_bit_tests(cuda, monkeypatch, dtype, C, H, W, R):
+    """The compile-time half-plane form of the grad_w kernel and its
+    per-entry bit-test form perform the same operations: equal bit for bit."""
+    torch.manual_seed(R)
+    sh = torch.tensor(O.halfplane_shifts(R))
+    S, B = sh.shape[0], 2
+    x = torch.rand(B, C, H, W).to(dtype)
+    w = torch.rand(S * B, 1, H, W).to(dtype)
+    gU, gZ = torch.randn(B, C, H, W), torch.randn(B, C, H, W)
+    _, gw = _grads(x, w, sh, gU, gZ, cuda)
+    monkeypatch.setenv("NSC_GW_GENERIC", "1")
+    _, gw2 = _grads(x, w, sh, gU, gZ, cuda)
+    assert torch.equal(gw, gw2)
+
+
 @pytest.mark.parametrize("dtype,C,Cw,H,W,table,logw,periodic", [
     (torch.float32, 3, 1, 40, 64, ("window", 7), True, False),    # GASD family
     (torch.float32, 1, 1, 30, 48, ("half", 5), True, False),      # NECTR family
