@@ -93,12 +93,13 @@ __device__ __forceinline__ void load_row(float (&d)[N], const float* p) {
     }
 }
 
-// EXACT: the table is the canonical half-plane table of radius R = tab.Rx
-// <= DYMAX (every dx in [-R, R] with dy = 1..R, all with mirror terms, plus
-// (dx, 0) for dx >= 0 with a mirror term for dx > 0), so whether an entry
-// exists and has a mirror term is a uniform test of the compile-time dy
-// against R (or of dx for dy = 0) instead of per-entry bit tests.
-template <typename T, int NC, int DYMIN, int DYMAX, bool EXACT>
+// PAT (entry pattern): 0 any table (per-entry bit tests); 1 the canonical
+// half-plane table of radius R = tab.Rx <= DYMAX (every dx in [-R, R] with
+// dy = 1..R, all with mirror terms, plus (dx, 0) for dx >= 0 with a mirror
+// term for dx > 0), so whether an entry exists and has a mirror term is a
+// uniform test of the compile-time dy against R (or of dx for dy = 0);
+// 2 the same table with R = DYMAX, where only the dy = 0 test is left.
+template <typename T, int NC, int DYMIN, int DYMAX, int PAT>
 __global__ void __launch_bounds__(NT)
 acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
               const float* __restrict__ gZ, T* __restrict__ gw, const GwTable tab,
@@ -167,12 +168,14 @@ acc_gw_kernel(const T* __restrict__ x, const float* __restrict__ gU,
         // entry j (dy = DYMIN + j) present / with a mirror term
         auto has = [&](auto jc) -> bool {
             constexpr int j = decltype(jc)::value;
-            if constexpr (EXACT) return j > 0 ? j <= Rx : dx >= 0;
+            if constexpr (PAT == 2) return j > 0 || dx >= 0;
+            else if constexpr (PAT == 1) return j > 0 ? j <= Rx : dx >= 0;
             else return (pres >> j) & 1u;
         };
         auto mir = [&](auto jc) -> bool {
             constexpr int j = decltype(jc)::value;
-            if constexpr (EXACT) return j > 0 ? j <= Rx : dx > 0;
+            if constexpr (PAT == 2) return j > 0 || dx > 0;
+            else if constexpr (PAT == 1) return j > 0 ? j <= Rx : dx > 0;
             else return (invm >> j) & 1u;
         };
         float acc[NDY][V];
@@ -354,10 +357,10 @@ acc_gx_kernel(const T* __restrict__ w, const float* __restrict__ gU,
     }
 }
 
-template <typename T, int NC, int LO, int HI, bool EXACT>
+template <typename T, int NC, int LO, int HI, int PAT>
 bool launch(const void* x, const void* gU, const void* gZ, void* gw, const GwTable& tab,
             const GwGeo& g, size_t smem, dim3 grid, cudaStream_t stream) {
-    auto k = acc_gw_kernel<T, NC, LO, HI, EXACT>;
+    auto k = acc_gw_kernel<T, NC, LO, HI, PAT>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess) {
         cudaGetLastError();
@@ -369,18 +372,19 @@ bool launch(const void* x, const void* gU, const void* gZ, void* gw, const GwTab
 }
 
 template <typename T, int NC>
-bool by_range(bool exact, int lo, int hi, const void* x, const void* gU, const void* gZ,
+bool by_range(int pat, int lo, int hi, const void* x, const void* gU, const void* gZ,
               void* gw, const GwTable& tab, const GwGeo& g, size_t smem, dim3 grid,
               cudaStream_t st) {
-#define NSC_GW(L, H)                                                                    \
-    if (lo == L && hi == H)                                                           \
-        return exact ? launch<T, NC, L, H, true>(x, gU, gZ, gw, tab, g, smem, grid, st) \
-                     : launch<T, NC, L, H, false>(x, gU, gZ, gw, tab, g, smem, grid, st);
+#define NSC_GW(L, H)                                                                   \
+    if (lo == L && hi == H)                                                          \
+        return pat == 2 ? launch<T, NC, L, H, 2>(x, gU, gZ, gw, tab, g, smem, grid, st) \
+             : pat == 1 ? launch<T, NC, L, H, 1>(x, gU, gZ, gw, tab, g, smem, grid, st) \
+                        : launch<T, NC, L, H, 0>(x, gU, gZ, gw, tab, g, smem, grid, st);
     NSC_GW(0, 2) NSC_GW(0, 4) NSC_GW(0, 6) NSC_GW(0, 8) NSC_GW(0, 10) NSC_GW(0, 12)
 #undef NSC_GW
     // tables reaching negative dy are never canonical half-plane tables
-    if (lo == -4 && hi == 4) return launch<T, NC, -4, 4, false>(x, gU, gZ, gw, tab, g, smem, grid, st);
-    if (lo == -6 && hi == 6) return launch<T, NC, -6, 6, false>(x, gU, gZ, gw, tab, g, smem, grid, st);
+    if (lo == -4 && hi == 4) return launch<T, NC, -4, 4, 0>(x, gU, gZ, gw, tab, g, smem, grid, st);
+    if (lo == -6 && hi == 6) return launch<T, NC, -6, 6, 0>(x, gU, gZ, gw, tab, g, smem, grid, st);
     return false;
 }
 
@@ -410,7 +414,7 @@ bool gx_by_range(int lo, int hi, const void* w, const void* gU, void* gx,
     return false;
 }
 
-inline bool dispatch(int xd, int NC, bool exact, int lo, int hi, const void* x,
+inline bool dispatch(int xd, int NC, int exact, int lo, int hi, const void* x,
                      const void* gU, const void* gZ, void* gw, const GwTable& tab,
                      const GwGeo& g, size_t smem, dim3 grid, cudaStream_t st) {
     if (xd == NSC_F16)
@@ -497,7 +501,7 @@ bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C
     const dim3 grid(static_cast<unsigned>(g.tiles_x * g.tiles_y),
                     static_cast<unsigned>(B * (Cw == 1 ? 1 : C)));
     // canonical half-plane table of radius R = tab.Rx <= hi (acc_gw_kernel's
-    // EXACT): every present / mirror bit as the pattern says, nothing else
+    // PAT 1, or PAT 2 when R == hi): every present / mirror bit as the pattern says, nothing else
     const int R = tab.Rx;
     bool exact = lo == 0 && R >= 1 && R <= hi;
     for (int dx = -R; exact && dx <= R; ++dx) {
@@ -509,8 +513,8 @@ bool acc_gw_fast(const void* x, int xd, int wd, int64_t Cw, int64_t B, int64_t C
         }
         exact = tab.present[dx + MAXR] == pres && tab.inv[dx + MAXR] == mir;
     }
-    if (std::getenv("NSC_GW_GENERIC")) exact = false;
-    return gwk::dispatch(xd, NC, exact, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, stream);
+    const int pat = std::getenv("NSC_GW_GENERIC") ? 0 : !exact ? 0 : R == hi ? 2 : 1;
+    return gwk::dispatch(xd, NC, pat, lo, hi, x, gU, gZ, gw, tab, g, smem, grid, stream);
 }
 
 bool acc_gx_fast(const void* w, int xd, int wd, int64_t Cw, int64_t B, int64_t C,
