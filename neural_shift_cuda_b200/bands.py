@@ -224,7 +224,17 @@ def exchange_start(x_pad: torch.Tensor, R: int, top, bot, group=None,
     # Messages between a pair match in issue order (with two ranks `up` and
     # `down` are the same peer): every rank sends last rows, first rows, top
     # strip, bottom strip, and receives in the matching order.
-    if halo:
+    direct = halo and x_pad.is_contiguous()
+    if direct:
+        # each (image, channel) plane's halo rows are contiguous: send the
+        # band's rows straight from x_pad and receive into its spare rows
+        planes = [x_pad[b, c] for b in range(x_pad.shape[0])
+                  for c in range(x_pad.shape[1])]
+        sends += [(p[Hb:Hb + R], down) for p in planes]          # last R rows
+        sends += [(p[R:2 * R], up) for p in planes]              # first R rows
+        recvs += [(p[:R], up) for p in planes]
+        recvs += [(p[R + Hb:], down) for p in planes]
+    elif halo:
         first = x_pad[:, :, R:2 * R].contiguous()      # this band's first R rows
         last = x_pad[:, :, Hb:Hb + R].contiguous()     # this band's last R rows
         from_up = torch.empty_like(last)
@@ -262,7 +272,7 @@ def exchange_start(x_pad: torch.Tensor, R: int, top, bot, group=None,
                 raise BandExchangeError(
                     f"rank {rank}: band exchange with ranks {up} / {down} did not "
                     f"complete within {deadline} s")
-        if halo:
+        if halo and not direct:
             x_pad[:, :, :R] = from_up
             x_pad[:, :, R + Hb:] = from_down
         return from_below, from_above
@@ -271,7 +281,7 @@ def exchange_start(x_pad: torch.Tensor, R: int, top, bot, group=None,
 
 def _reserve_sms() -> int:
     import os
-    return int(os.environ.get("NSC_BAND_RESERVE_SMS", "2"))
+    return int(os.environ.get("NSC_BAND_RESERVE_SMS", "0"))
 
 
 def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
@@ -339,7 +349,8 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
                         dtype=acc, device=x_pad.device)
         Z = torch.empty_like(U)
         nsm = torch.cuda.get_device_properties(x_pad.device).multi_processor_count
-        cap = max(1, nsm - _reserve_sms()) if world > 1 else 0
+        reserve = _reserve_sms()
+        cap = max(1, nsm - reserve) if world > 1 and reserve > 0 else 0
         band_rows_cuda(x_pad, w_band, shifts, row0, Hg, 0, Hb, U, Z, cap)
         from_below, from_above = finish_strips()
     else:

@@ -16,6 +16,7 @@
 // The tiled TMA kernel in accumulate_fast.cuh takes over the forward when the
 // geometry allows it; this file is the general path (any W, any alignment).
 
+#include <algorithm>
 #include <cstdlib>
 
 #include "nsc_common.cuh"
@@ -103,13 +104,19 @@ acc_fwd_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
 // Mirror contributions of the band's own weights to the R rows outside it.
 // Each strip is (2, B, C, R, W); part 0 = U, part 1 = Z; the top strip
 // targets rows row0-R .. row0-1, the bottom strip the R rows below the band.
-// Both strips in one launch, the shift loop split over kKS thread groups:
-// threadIdx.y takes every kKS-th shift and the partial sums meet in shared
-// memory.  blockIdx.y enumerates the 2R strip rows (top strip first).
-// The shifts that can reach each strip row (has_inv and a mirror source
-// row inside the band) are listed on the host, so a thread visits only
-// those: for row t above the band, rows with dx <= t; below, dx > t - Hb.
-constexpr int kKS = 8;
+// Both strips in one launch: a block owns kEX columns of one strip row
+// (blockIdx.y enumerates the 2R strip rows, top strip first) and splits the
+// row's shift list over kEK thread groups, whose partial sums meet in shared
+// memory in a fixed order.  The shifts that can reach each strip row (has_inv
+// and a mirror source row inside the band) are listed on the host, so a
+// thread visits only those: for row t above the band, rows with dx <= t;
+// below, dx > t - Hb.  The block stages, per listed shift, the element
+// offsets of its mirror source row (weight plane and row, x row) and dy in
+// shared memory, so the shift loop is a few adds and four loads; every load
+// of an unrolled group is issued unconditionally (an out-of-image column
+// reads the row's column 0 and the term is dropped by a select), so eight
+// shifts' loads are in flight together.
+constexpr int kEX = 64, kEK = 4;
 constexpr int kEdgeRows = 64;        // 2R strip rows, R <= 32
 constexpr int kEdgeList = 4096;
 struct EdgeLists {
@@ -118,23 +125,40 @@ struct EdgeLists {
 };
 
 template <typename TX, typename TW, int NC>
-__global__ void __launch_bounds__(kBX * kKS)
-acc_edges2_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
-                  typename Acc<TX>::type* __restrict__ top_out,
-                  typename Acc<TX>::type* __restrict__ bot_out, const ShiftTable st,
-                  const EdgeLists lists,
-                  int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t Cw,
-                  int64_t R, int64_t row0, int64_t Hg, int64_t groups) {
+__global__ void __launch_bounds__(kEX * kEK)
+acc_edges_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
+                 typename Acc<TX>::type* __restrict__ top_out,
+                 typename Acc<TX>::type* __restrict__ bot_out, const ShiftTable st,
+                 const EdgeLists lists,
+                 int64_t B, int64_t C, int64_t Hb, int64_t W, int64_t Cw,
+                 int64_t R, int64_t row0, int64_t Hg, int64_t groups) {
     using A = typename Acc<TX>::type;
-    __shared__ A part[kKS][NC + 1][kBX];
-    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kBX + threadIdx.x;
+    extern __shared__ __align__(16) unsigned char edge_smem[];
+    const int rr = blockIdx.y;
+    const int j0 = lists.off[rr];
+    const int n = lists.off[rr + 1] - j0;
+    int64_t* woff = reinterpret_cast<int64_t*>(edge_smem);
+    int64_t* xoff = woff + n;
+    int32_t* dys = reinterpret_cast<int32_t*>(xoff + n);
+    __shared__ A part[kEK][NC + 1][kEX];
     const int k = threadIdx.y;
-    const bool top = blockIdx.y < R;
-    const int64_t e = top ? blockIdx.y : blockIdx.y - R;
+    const int tid = k * kEX + threadIdx.x;
+    const bool top = rr < R;
+    const int64_t e = top ? rr : rr - R;
     const int64_t t = top ? (e - R) : (Hb + e);   // target row, band-local
     const int64_t plane_x = (Hb + 2 * R) * W;
     const int64_t plane_o = Hb * W;
     const int64_t plane_e = R * W;
+    const int64_t wstride = B * Cw * plane_o;     // one shift plane
+    for (int i = tid; i < n; i += kEX * kEK) {
+        const int s = lists.s[j0 + i];
+        const int64_t ro = (t - st.dx[s]) * W - st.dy[s];   // mirror row, column -dy
+        woff[i] = s * wstride + ro;
+        xoff[i] = ro;
+        dys[i] = st.dy[s];
+    }
+    __syncthreads();
+    const int64_t wcol = static_cast<int64_t>(blockIdx.x) * kEX + threadIdx.x;
     const int64_t cgroups = (Cw == 1) ? (C + NC - 1) / NC : C;
     const bool active = wcol < W && inb(row0 + t, Hg);
     A* out = top ? top_out : bot_out;
@@ -144,23 +168,27 @@ acc_edges2_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
         const int64_t c0 = (Cw == 1) ? cg * NC : cg;
         const int64_t wc = (Cw == 1) ? 0 : cg;
         const int nc = (Cw == 1) ? static_cast<int>(C - c0 < NC ? C - c0 : NC) : 1;
-        const TX* xb = x + (b * C + c0) * plane_x;
+        const TW* wb = w + (b * Cw + wc) * plane_o + wcol;
+        const TX* xc[NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i)   // band row 0 of channel c0 + i (clamped)
+            xc[i] = x + (b * C + c0 + (i < nc ? i : 0)) * plane_x + R * W + wcol;
         A u[NC], z = A(0);
 #pragma unroll
         for (int i = 0; i < NC; ++i) u[i] = A(0);
         if (active) {
-            const int j1 = lists.off[blockIdx.y + 1];
-#pragma unroll 4
-            for (int j = lists.off[blockIdx.y] + k; j < j1; j += kKS) {
-                const int s = lists.s[j];
-                const int64_t hm = t - st.dx[s], wm = wcol - st.dy[s];
-                if (!inb(wm, W)) continue;
-                const TW* ws = w + ((static_cast<int64_t>(s) * B + b) * Cw + wc) * plane_o;
-                const A mv = ldg_acc<TW, A>(ws + hm * W + wm);
-                const int64_t mo = (hm + R) * W + wm;
+#pragma unroll 8
+            for (int j = k; j < n; j += kEK) {
+                const int dy = dys[j];
+                const bool ok = static_cast<uint64_t>(wcol - dy) < static_cast<uint64_t>(W);
+                const int64_t adj = ok ? 0 : dy - wcol;
+                const A mv0 = ldg_acc<TW, A>(wb + woff[j] + adj);
+                A xv[NC];
 #pragma unroll
-                for (int i = 0; i < NC; ++i)
-                    if (i < nc) u[i] += mv * ldg_acc<TX, A>(xb + i * plane_x + mo);
+                for (int i = 0; i < NC; ++i) xv[i] = ldg_acc<TX, A>(xc[i] + xoff[j] + adj);
+                const A mv = ok ? mv0 : A(0);
+#pragma unroll
+                for (int i = 0; i < NC; ++i) u[i] += mv * (ok ? xv[i] : A(0));
                 z += mv;
             }
         }
@@ -174,7 +202,8 @@ acc_edges2_kernel(const TX* __restrict__ x, const TW* __restrict__ w,
 #pragma unroll
             for (int i = 0; i <= NC; ++i) {
                 su[i] = A(0);
-                for (int j = 0; j < kKS; ++j) su[i] += part[j][i][threadIdx.x];
+#pragma unroll
+                for (int j = 0; j < kEK; ++j) su[i] += part[j][i][threadIdx.x];
             }
             const int64_t ob = (b * C + c0) * plane_e + e * W + wcol;
             const int64_t zoff = B * C * plane_e;
@@ -567,6 +596,10 @@ nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
         }
     }
     lists.off[2 * R] = n;
+    int maxn = 0;
+    for (int64_t rr = 0; rr < 2 * R; ++rr)
+        maxn = std::max(maxn, lists.off[rr + 1] - lists.off[rr]);
+    const size_t smem = static_cast<size_t>(maxn) * 20;   // woff, xoff, dy
     return with_types("accumulate_uz_band_edges", xd, wd, [&](auto tx, auto tw) {
         using TX = std::remove_const_t<std::remove_pointer_t<decltype(tx)>>;
         using TW = std::remove_const_t<std::remove_pointer_t<decltype(tw)>>;
@@ -575,9 +608,9 @@ nsc_status acc_edges(const void* x, int xd, const void* w, int wd, int64_t Cw,
         with_nc(C, Cw, [&](auto tag) {
             constexpr int NC = decltype(tag)::value_nc;
             const int64_t groups = n_groups(B, C, Cw, NC);
-            const dim3 grid(grid_1d(W, kBX), static_cast<unsigned>(2 * R),
+            const dim3 grid(grid_1d(W, kEX), static_cast<unsigned>(2 * R),
                             static_cast<unsigned>(groups < 65535 ? groups : 65535));
-            acc_edges2_kernel<TX, TW, NC><<<grid, dim3(kBX, kKS), 0, stream>>>(
+            acc_edges_kernel<TX, TW, NC><<<grid, dim3(kEX, kEK), smem, stream>>>(
                 static_cast<const TX*>(x), static_cast<const TW*>(w),
                 static_cast<A*>(top), static_cast<A*>(bot), st, lists, B, C, Hb, W,
                 Cw, R, row0, Hg, groups);
