@@ -476,12 +476,33 @@ nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype, int64_t w_channel
                 if (!tile_smem(ka, tg, mtile::kBwdAF<A, NC>, sizeof(A), &sa) ||
                     !tile_smem(kb, tg, mtile::kBwdBF<A, NC>, sizeof(A), &sb))
                     return;
-                ka<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sa, sm>>>(
-                    static_cast<const T*>(w_half), static_cast<const T*>(img),
-                    static_cast<const A*>(degree), static_cast<const T*>(d_hat),
-                    static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),
-                    static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st, tg,
-                    use_box ? 1 : 0, static_cast<A>(eps));
+                bool packed = false;
+                if constexpr (std::is_same_v<A, float> && mtile::PPT == 2) {
+                    // fp32: the thread's two pixels as f32x2 lanes
+                    auto k2 = mtile::bwd_a_tile_x2<T, NC>;
+                    const size_t s2 = sizeof(mtile::PRec<NC>) *
+                                      static_cast<size_t>(mtile::TY + 2 * tg.R) * tg.XP;
+                    if (s2 <= 200 * 1024 &&
+                        (s2 <= 48 * 1024 ||
+                         cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(s2)) == cudaSuccess)) {
+                        k2<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), s2, sm>>>(
+                            static_cast<const T*>(w_half), static_cast<const T*>(img),
+                            static_cast<const A*>(degree), static_cast<const T*>(d_hat),
+                            static_cast<const T*>(grad_Wx),
+                            static_cast<const T*>(grad_d_hat),
+                            static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st,
+                            tg, use_box ? 1 : 0, static_cast<A>(eps));
+                        packed = true;
+                    }
+                }
+                if (!packed)
+                    ka<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sa, sm>>>(
+                        static_cast<const T*>(w_half), static_cast<const T*>(img),
+                        static_cast<const A*>(degree), static_cast<const T*>(d_hat),
+                        static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),
+                        static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st, tg,
+                        use_box ? 1 : 0, static_cast<A>(eps));
                 kb<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sb, sm>>>(
                     static_cast<const T*>(img), static_cast<const A*>(degree),
                     static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),

@@ -440,6 +440,220 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
     }
 }
 
+// Packed fp32 pairs: the two pixels a thread owns (rows TY apart) run as
+// the two lanes of sm_100's f32x2 arithmetic, one instruction per pair.
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{.reg .b64 a,b,c,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5}; mov.b64 c,{%6,%7};"
+        " fma.rn.f32x2 d,a,b,c; mov.b64 {%0,%1},d;}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 a,b,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5};"
+        " mul.rn.f32x2 d,a,b; mov.b64 {%0,%1},d;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 a,b,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5};"
+        " add.rn.f32x2 d,a,b; mov.b64 {%0,%1},d;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+// -share(self, other) where the denominator passes gradient (max >= eps),
+// else 0: the factor of a pair's degree-gradient term.
+__device__ __forceinline__ float neg_share(float self, float other, float eps) {
+    if (!((self > other ? self : other) >= eps)) return 0.f;
+    return self > other ? -1.f : (self == other ? -0.5f : 0.f);
+}
+
+// backward A for fp32 accumulators with the thread's two pixels packed.
+// Records hold pixel PAIRS: pair row i of the staged halo holds halo rows i
+// and i + TY side by side (field k of both rows in one float2), so the
+// neighbour records of both pixels, at the same offset (dx, dy), are one
+// record.  Same terms, order and special cases as bwd_a_tile, except that a
+// box-masked or zero weight contributes its (zero) products instead of
+// being skipped -- identical for finite inputs.
+template <int NC> constexpr int kBwdA2F = (3 + 2 * NC + 1) / 2 * 2;
+template <int NC>
+struct alignas(16) PRec {
+    float2 f[kBwdA2F<NC>];
+};
+
+template <typename T, int NC>
+__global__ void __launch_bounds__(NT)
+bwd_a_tile_x2(const T* __restrict__ w, const T* __restrict__ x,
+              const float* __restrict__ d, const T* __restrict__ dhat,
+              const T* __restrict__ gWx, const T* __restrict__ gdh,
+              float* __restrict__ gd, T* __restrict__ gx,
+              const ShiftTable st, const Geo g, int use_box, float eps) {
+    static_assert(PPT == 2, "two pixels per thread");
+    constexpr int F = kBwdA2F<NC>;
+    constexpr int XO = 3, GO = 3 + NC;
+    extern __shared__ __align__(16) unsigned char smem_m[];
+    PRec<NC>* rec = reinterpret_cast<PRec<NC>*>(smem_m);
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    const int PR = TY + 2 * g.R;   // pair rows
+    const int tid = threadIdx.y * TX + threadIdx.x;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
+            __syncthreads();
+            const float* dg = d + grp * HW;
+            for (int idx = tid; idx < PR * g.XP; idx += NT) {
+                const int i = idx / g.XP;
+                const int j = idx - i * g.XP;
+                const int c = pmod(o.w0 - g.R + j, g.W);
+                PRec<NC> r;
+#pragma unroll
+                for (int k = 0; k < F; ++k) r.f[k] = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int64_t off =
+                        static_cast<int64_t>(pmod(o.h0 - g.R + i + hh * TY, g.H)) * g.W + c;
+                    float v[3 + 2 * NC];
+                    const float dv = dg[off];
+                    v[0] = dv;
+                    v[1] = 1.f / (dv > eps ? dv : eps);
+                    float a = 0.f;
+#pragma unroll
+                    for (int cc = 0; cc < NC; ++cc) {
+                        const float xv = to_acc(x[cb + cc * HW + off]);
+                        const float gv = to_acc(gWx[cb + cc * HW + off]);
+                        v[XO + cc] = xv;
+                        v[GO + cc] = gv;
+                        a += to_acc(gdh[cb + cc * HW + off]) - gv * xv;
+                    }
+                    v[2] = a;
+#pragma unroll
+                    for (int k = 0; k < 3 + 2 * NC; ++k) {
+                        if (hh == 0) r.f[k].x = v[k];
+                        else r.f[k].y = v[k];
+                    }
+                }
+                rec[idx] = r;
+            }
+            __syncthreads();
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            const T* wb = w + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            int hh[2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                hh[p] = h < g.H ? h : g.H - 1;
+            }
+            const int ci = (threadIdx.y + g.R) * g.XP + threadIdx.x + g.R;
+            float2 di, ri, aq, xq[NC], gq[NC], gxa[NC];
+            float2 g_d = make_float2(0.f, 0.f);
+            {
+                const PRec<NC> me = rec[ci];
+                di = me.f[0];
+                ri = me.f[1];
+                aq = me.f[2];
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    xq[c] = me.f[XO + c];
+                    gq[c] = me.f[GO + c];
+                    const int64_t q0 = static_cast<int64_t>(hh[0]) * g.W + wcol;
+                    const int64_t q1 = static_cast<int64_t>(hh[1]) * g.W + wcol;
+                    gxa[c] = make_float2(
+                        gq[c].x * (1.f - static_cast<float>(to_acc(dhat[cb + c * HW + q0]))),
+                        gq[c].y * (1.f - static_cast<float>(to_acc(dhat[cb + c * HW + q1]))));
+                }
+            }
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 1
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const int off = dx * g.XP + dy;
+                    const T* ws = wb + s * sstride;
+                    const EdgeGeom e0 = edge_geom<BORDER>(g, hh[0], wcol, dx, dy);
+                    const EdgeGeom e1 = edge_geom<BORDER>(g, hh[1], wcol, dx, dy);
+                    float2 wq = make_float2(ldg_acc<T, float>(ws + e0.q),
+                                            ldg_acc<T, float>(ws + e1.q));
+                    float2 wm = make_float2(ldg_acc<T, float>(ws + e0.m),
+                                            ldg_acc<T, float>(ws + e1.m));
+                    if (BORDER && use_box) {
+                        if (!e0.in_p) wq.x = 0.f;
+                        if (!e1.in_p) wq.y = 0.f;
+                        if (!e0.in_m) wm.x = 0.f;
+                        if (!e1.in_m) wm.y = 0.f;
+                    }
+                    // Pair (q, q + d), weight w_s(q): own forward edge of q
+                    // and (inv) the mirror edge of q + d ending at q.
+                    {
+                        const PRec<NC> nb = rec[ci + off];
+                        const float2 dn = nb.f[0];
+                        const float2 r = make_float2(fminf(ri.x, nb.f[1].x),
+                                                     fminf(ri.y, nb.f[1].y));
+                        float2 Tq = aq, Tn = make_float2(0.f, 0.f);
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) Tq = f2fma(gq[c], nb.f[XO + c], Tq);
+                        if (inv) {
+                            const float2 wk = f2mul(wq, r);
+                            Tn = nb.f[2];
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) {
+                                const float2 gn = nb.f[GO + c];
+                                Tn = f2fma(gn, xq[c], Tn);
+                                gxa[c] = f2fma(gn, wk, gxa[c]);
+                            }
+                        }
+                        const float2 t = f2mul(f2mul(f2mul(f2add(Tq, Tn), wq), r), r);
+                        g_d = f2fma(t, make_float2(neg_share(di.x, dn.x, eps),
+                                                   neg_share(di.y, dn.y, eps)), g_d);
+                    }
+                    // Pair (q, q - d), weight w_s(q - d): forward edge of
+                    // q - d ending at q and (inv) the own mirror edge of q.
+                    {
+                        const PRec<NC> nb = rec[ci - off];
+                        const float2 dn = nb.f[0];
+                        const float2 r = make_float2(fminf(ri.x, nb.f[1].x),
+                                                     fminf(ri.y, nb.f[1].y));
+                        const float2 wk = f2mul(wm, r);
+                        float2 Tn = nb.f[2], Tq = make_float2(0.f, 0.f);
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) {
+                            const float2 gn = nb.f[GO + c];
+                            Tn = f2fma(gn, xq[c], Tn);
+                            gxa[c] = f2fma(gn, wk, gxa[c]);
+                        }
+                        if (inv) {
+                            Tq = aq;
+#pragma unroll
+                            for (int c = 0; c < NC; ++c) Tq = f2fma(gq[c], nb.f[XO + c], Tq);
+                        }
+                        const float2 t = f2mul(f2mul(f2mul(f2add(Tn, Tq), wm), r), r);
+                        g_d = f2fma(t, make_float2(neg_share(di.x, dn.x, eps),
+                                                   neg_share(di.y, dn.y, eps)), g_d);
+                    }
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                if (h >= g.H) continue;
+                const int64_t q = static_cast<int64_t>(h) * g.W + wcol;
+                gd[grp * HW + q] = p == 0 ? g_d.x : g_d.y;
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    gx[cb + c * HW + q] = static_cast<T>(p == 0 ? gxa[c].x : gxa[c].y);
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------ backward B
 // grad_w without reading w:
 //   gw_s(q) = keep_f(q) (G_f r + g_d(q)) + inv keep_i(q + d) (G_m r + g_d(q + d))
