@@ -384,6 +384,19 @@ bool tile_smem(K kern, const mtile::Geo& g, int planes, size_t elem, size_t* byt
     return true;
 }
 
+// Dynamic shared memory of a packed (pixel-pair record) tiled kernel:
+// TY + 2R pair rows of XP records of `rec_bytes`.
+template <typename K>
+bool pair_smem(K kern, const mtile::Geo& g, size_t rec_bytes, size_t* bytes) {
+    *bytes = rec_bytes * static_cast<size_t>(mtile::TY + 2 * g.R) * g.XP;
+    if (*bytes > 200 * 1024) return false;
+    if (*bytes > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(*bytes)) != cudaSuccess)
+        return false;
+    return true;
+}
+
 }  // namespace
 }  // namespace nsc
 
@@ -480,12 +493,10 @@ nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype, int64_t w_channel
                 if constexpr (std::is_same_v<A, float> && mtile::PPT == 2) {
                     // fp32: the thread's two pixels as f32x2 lanes
                     auto k2 = mtile::bwd_a_tile_x2<T, NC>;
-                    const size_t s2 = sizeof(mtile::PRec<NC>) *
-                                      static_cast<size_t>(mtile::TY + 2 * tg.R) * tg.XP;
-                    if (s2 <= 200 * 1024 &&
-                        (s2 <= 48 * 1024 ||
-                         cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(s2)) == cudaSuccess)) {
+                    auto k2b = mtile::bwd_b_tile_x2<T, NC>;
+                    size_t s2 = 0, s2b = 0;
+                    if (pair_smem(k2, tg, sizeof(mtile::PRec<NC>), &s2) &&
+                        pair_smem(k2b, tg, sizeof(mtile::PRF<mtile::kBwdB2F<NC>>), &s2b)) {
                         k2<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), s2, sm>>>(
                             static_cast<const T*>(w_half), static_cast<const T*>(img),
                             static_cast<const A*>(degree), static_cast<const T*>(d_hat),
@@ -493,16 +504,25 @@ nsc_status nsc_metropolis_bwd(const void* w_half, int w_dtype, int64_t w_channel
                             static_cast<const T*>(grad_d_hat),
                             static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st,
                             tg, use_box ? 1 : 0, static_cast<A>(eps));
+                        k2b<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), s2b, sm>>>(
+                            static_cast<const T*>(img), static_cast<const A*>(degree),
+                            static_cast<const T*>(grad_Wx),
+                            static_cast<const T*>(grad_d_hat),
+                            static_cast<const A*>(grad_degree), static_cast<T*>(grad_w),
+                            st, tg, use_box ? 1 : 0, static_cast<A>(eps));
                         packed = true;
                     }
                 }
-                if (!packed)
-                    ka<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sa, sm>>>(
-                        static_cast<const T*>(w_half), static_cast<const T*>(img),
-                        static_cast<const A*>(degree), static_cast<const T*>(d_hat),
-                        static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),
-                        static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st, tg,
-                        use_box ? 1 : 0, static_cast<A>(eps));
+                if (packed) {
+                    launched = true;
+                    return;
+                }
+                ka<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sa, sm>>>(
+                    static_cast<const T*>(w_half), static_cast<const T*>(img),
+                    static_cast<const A*>(degree), static_cast<const T*>(d_hat),
+                    static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),
+                    static_cast<A*>(grad_degree), static_cast<T*>(grad_img), st, tg,
+                    use_box ? 1 : 0, static_cast<A>(eps));
                 kb<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), sb, sm>>>(
                     static_cast<const T*>(img), static_cast<const A*>(degree),
                     static_cast<const T*>(grad_Wx), static_cast<const T*>(grad_d_hat),

@@ -478,11 +478,43 @@ __device__ __forceinline__ float neg_share(float self, float other, float eps) {
 // record.  Same terms, order and special cases as bwd_a_tile, except that a
 // box-masked or zero weight contributes its (zero) products instead of
 // being skipped -- identical for finite inputs.
-template <int NC> constexpr int kBwdA2F = (3 + 2 * NC + 1) / 2 * 2;
-template <int NC>
-struct alignas(16) PRec {
-    float2 f[kBwdA2F<NC>];
+template <int F>
+struct alignas(16) PRF {
+    float2 f[F];
 };
+template <int NC> constexpr int kBwdA2F = (3 + 2 * NC + 1) / 2 * 2;
+template <int NC> using PRec = PRF<kBwdA2F<NC>>;
+
+// Stages pixel-pair records over the tile's halo: pair row i holds halo
+// rows i and i + TY; fill(off, v) writes the fields of the pixel at plane
+// offset off into v[0 .. F).
+template <int F, typename Fill>
+__device__ __forceinline__ void stage_pairs(const Geo& g, const Where& o, PRF<F>* rec,
+                                            Fill&& fill) {
+    const int PR = TY + 2 * g.R;
+    const int tid = threadIdx.y * TX + threadIdx.x;
+    for (int idx = tid; idx < PR * g.XP; idx += NT) {
+        const int i = idx / g.XP;
+        const int j = idx - i * g.XP;
+        const int c = pmod(o.w0 - g.R + j, g.W);
+        PRF<F> r;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int64_t off =
+                static_cast<int64_t>(pmod(o.h0 - g.R + i + hh * TY, g.H)) * g.W + c;
+            float v[F];
+#pragma unroll
+            for (int k = 0; k < F; ++k) v[k] = 0.f;
+            fill(off, v);
+#pragma unroll
+            for (int k = 0; k < F; ++k) {
+                if (hh == 0) r.f[k].x = v[k];
+                else r.f[k].y = v[k];
+            }
+        }
+        rec[idx] = r;
+    }
+}
 
 template <typename T, int NC>
 __global__ void __launch_bounds__(NT)
@@ -498,47 +530,27 @@ bwd_a_tile_x2(const T* __restrict__ w, const T* __restrict__ x,
     PRec<NC>* rec = reinterpret_cast<PRec<NC>*>(smem_m);
     const int64_t HW = static_cast<int64_t>(g.H) * g.W;
     const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
-    const int PR = TY + 2 * g.R;   // pair rows
-    const int tid = threadIdx.y * TX + threadIdx.x;
     for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
         for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
             const Where o = where(g, tile, grp);
             const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
             __syncthreads();
             const float* dg = d + grp * HW;
-            for (int idx = tid; idx < PR * g.XP; idx += NT) {
-                const int i = idx / g.XP;
-                const int j = idx - i * g.XP;
-                const int c = pmod(o.w0 - g.R + j, g.W);
-                PRec<NC> r;
+            stage_pairs<F>(g, o, rec, [&](int64_t off, float* v) {
+                const float dv = dg[off];
+                v[0] = dv;
+                v[1] = 1.f / (dv > eps ? dv : eps);
+                float a = 0.f;
 #pragma unroll
-                for (int k = 0; k < F; ++k) r.f[k] = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int64_t off =
-                        static_cast<int64_t>(pmod(o.h0 - g.R + i + hh * TY, g.H)) * g.W + c;
-                    float v[3 + 2 * NC];
-                    const float dv = dg[off];
-                    v[0] = dv;
-                    v[1] = 1.f / (dv > eps ? dv : eps);
-                    float a = 0.f;
-#pragma unroll
-                    for (int cc = 0; cc < NC; ++cc) {
-                        const float xv = to_acc(x[cb + cc * HW + off]);
-                        const float gv = to_acc(gWx[cb + cc * HW + off]);
-                        v[XO + cc] = xv;
-                        v[GO + cc] = gv;
-                        a += to_acc(gdh[cb + cc * HW + off]) - gv * xv;
-                    }
-                    v[2] = a;
-#pragma unroll
-                    for (int k = 0; k < 3 + 2 * NC; ++k) {
-                        if (hh == 0) r.f[k].x = v[k];
-                        else r.f[k].y = v[k];
-                    }
+                for (int cc = 0; cc < NC; ++cc) {
+                    const float xv = to_acc(x[cb + cc * HW + off]);
+                    const float gv = to_acc(gWx[cb + cc * HW + off]);
+                    v[XO + cc] = xv;
+                    v[GO + cc] = gv;
+                    a += to_acc(gdh[cb + cc * HW + off]) - gv * xv;
                 }
-                rec[idx] = r;
-            }
+                v[2] = a;
+            });
             __syncthreads();
             const int wcol = o.w0 + threadIdx.x;
             if (wcol >= g.W) continue;
@@ -650,6 +662,107 @@ bwd_a_tile_x2(const T* __restrict__ w, const T* __restrict__ x,
                 for (int c = 0; c < NC; ++c)
                     gx[cb + c * HW + q] = static_cast<T>(p == 0 ? gxa[c].x : gxa[c].y);
             }
+        }
+    }
+}
+
+// Backward B for fp32 accumulators, packed as in bwd_a_tile_x2 (records: d,
+// r, a, g_d, x[NC], gWx[NC]).
+template <int NC> constexpr int kBwdB2F = (4 + 2 * NC + 1) / 2 * 2;
+template <typename T, int NC>
+__global__ void __launch_bounds__(NT)
+bwd_b_tile_x2(const T* __restrict__ x, const float* __restrict__ d,
+              const T* __restrict__ gWx, const T* __restrict__ gdh,
+              const float* __restrict__ gd, T* __restrict__ gw,
+              const ShiftTable st, const Geo g, int use_box, float eps) {
+    static_assert(PPT == 2, "two pixels per thread");
+    constexpr int F = kBwdB2F<NC>;
+    constexpr int XO = 4, GO = 4 + NC;
+    extern __shared__ __align__(16) unsigned char smem_m[];
+    PRF<F>* rec = reinterpret_cast<PRF<F>*>(smem_m);
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
+            __syncthreads();
+            const float* dg = d + grp * HW;
+            const float* gdg = gd + grp * HW;
+            stage_pairs<F>(g, o, rec, [&](int64_t off, float* v) {
+                const float dv = dg[off];
+                v[0] = dv;
+                v[1] = 1.f / (dv > eps ? dv : eps);
+                float a = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < NC; ++cc) {
+                    const float xv = to_acc(x[cb + cc * HW + off]);
+                    const float gv = to_acc(gWx[cb + cc * HW + off]);
+                    v[XO + cc] = xv;
+                    v[GO + cc] = gv;
+                    a += to_acc(gdh[cb + cc * HW + off]) - gv * xv;
+                }
+                v[2] = a;
+                v[3] = gdg[off];
+            });
+            __syncthreads();
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            T* gwb = gw + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            int hh[2];
+            bool act[2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                act[p] = h < g.H;
+                hh[p] = act[p] ? h : g.H - 1;
+            }
+            const int ci = (threadIdx.y + g.R) * g.XP + threadIdx.x + g.R;
+            float2 ri, gdi, aq, xq[NC], gq[NC];
+            {
+                const PRF<F> me = rec[ci];
+                ri = me.f[1];
+                aq = me.f[2];
+                gdi = me.f[3];
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    xq[c] = me.f[XO + c];
+                    gq[c] = me.f[GO + c];
+                }
+            }
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 2
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const int off = dx * g.XP + dy;
+                    T* gws = gwb + s * sstride;
+                    const EdgeGeom e0 = edge_geom<BORDER>(g, hh[0], wcol, dx, dy);
+                    const EdgeGeom e1 = edge_geom<BORDER>(g, hh[1], wcol, dx, dy);
+                    const PRF<F> nb = rec[ci + off];
+                    const float2 r = make_float2(fminf(ri.x, nb.f[1].x),
+                                                 fminf(ri.y, nb.f[1].y));
+                    float2 G = aq;
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) G = f2fma(gq[c], nb.f[XO + c], G);
+                    float2 v = f2fma(G, r, gdi);
+                    if (inv) {
+                        float2 Gm = nb.f[2];
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) Gm = f2fma(nb.f[GO + c], xq[c], Gm);
+                        v = f2add(v, f2fma(Gm, r, nb.f[3]));
+                    }
+                    if (BORDER && use_box) {
+                        if (!e0.in_p) v.x = 0.f;
+                        if (!e1.in_p) v.y = 0.f;
+                    }
+                    if (act[0]) gws[e0.q] = static_cast<T>(v.x);
+                    if (act[1]) gws[e1.q] = static_cast<T>(v.y);
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
         }
     }
 }
