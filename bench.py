@@ -175,17 +175,22 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    vals = []
+    vals, dts = [], []
     for _ in range(args.warmup):
         cpu_reference(args.ref_rows)
     for _ in range(args.steps):
         v, threads, dt, desc = cpu_reference(args.ref_rows)
         vals.append(v)
+        dts.append(dt)
     v = statistics.median(vals)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": PIXEL_SHIFTS / v * 1e3, "higher_is_better": True,
+        # a step is one timed sample (the bounded band); the whole image at
+        # the sample's rate is reported beside it, not as the step time
+        "ms_per_step": statistics.median(dts) * 1e3,
+        "ms_full_workload_at_sample_rate": PIXEL_SHIFTS / v * 1e3,
+        "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": "accumulate_uz 8192x8192x3 R=10 S=221 (configs[4])",
