@@ -96,6 +96,27 @@ def test_fast_band_split(cuda, nb):
     torch.testing.assert_close(Zb, Z, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("B,C,Cw,W,R,dtype,nb", [
+    (2, 3, 3, 100, 3, torch.float32, 3),      # per-channel weights, general band path
+    (1, 5, 1, 72, 6, torch.bfloat16, 2),      # channel-shared, C > 4, two channel groups
+    (2, 2, 1, 160, 10, torch.float16, 4),     # R = 10 strips, 64-column blocks + ragged
+])
+def test_band_edges_shapes(cuda, B, C, Cw, W, R, dtype, nb):
+    """Edge strips across images, channel groups, widths that are not a
+    multiple of the kernel's 64-column block, and every storage dtype: the
+    banded result equals the unsplit op."""
+    H = 24 * nb
+    rows = O.halfplane_shifts(R)
+    sh = T(rows)
+    g = torch.Generator().manual_seed(B * 100 + W)
+    x = torch.rand(B, C, H, W, generator=g).to(dtype).to(cuda)
+    w = _w(len(rows), B, Cw, H, W, sh, dtype, W).to(cuda)
+    U, Z = nsc.accumulate_uz(x, w, sh)
+    Ub, Zb = bands.accumulate_uz_banded_local(x, w, sh, nb)
+    torch.testing.assert_close(Ub, U, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(Zb, Z, rtol=1e-5, atol=1e-5)
+
+
 def test_fullsize_config5_properties(cuda):
     """BASELINE configs[4] at full size: x fp16 (1,3,8192,8192), R=10
     (S=221), channel-shared fp16 weights.  With x = 1 every product is the
