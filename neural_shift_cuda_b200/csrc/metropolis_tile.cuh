@@ -582,7 +582,7 @@ bwd_a_tile_x2(const T* __restrict__ w, const T* __restrict__ x,
             }
             auto body = [&](auto border) {
                 constexpr bool BORDER = decltype(border)::value;
-#pragma unroll 1
+#pragma unroll 2
                 for (int s = 0; s < g.S; ++s) {
                     const int dx = st.dx[s], dy = st.dy[s];
                     const bool inv = st.has_inv(s);
