@@ -431,6 +431,20 @@ nsc_status nsc_metropolis_fwd(const void* w_half, int w_dtype, int64_t w_channel
                 mtile::degree_tile<T><<<tile_grid(tg), dim3(mtile::TX, mtile::TY), 0, sm>>>(
                     static_cast<const T*>(w_half), static_cast<A*>(degree), st, tg,
                     use_box ? 1 : 0);
+                if constexpr (std::is_same_v<A, float> && mtile::PPT == 2) {
+                    // fp32: the thread's two pixels as f32x2 lanes
+                    auto k2 = mtile::aggregate_tile_x2<T, NC>;
+                    size_t s2 = 0;
+                    if (pair_smem(k2, tg, sizeof(mtile::PRF<mtile::kAgg2F<NC>>), &s2)) {
+                        k2<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), s2, sm>>>(
+                            static_cast<const T*>(w_half), static_cast<const T*>(img),
+                            static_cast<const A*>(degree), static_cast<T*>(Wx),
+                            static_cast<T*>(d_hat), st, tg, use_box ? 1 : 0,
+                            static_cast<A>(eps));
+                        launched = true;
+                        return;
+                    }
+                }
                 agg<<<tile_grid(tg), dim3(mtile::TX, mtile::TY), smem, sm>>>(
                     static_cast<const T*>(w_half), static_cast<const T*>(img),
                     static_cast<const A*>(degree), static_cast<T*>(Wx),

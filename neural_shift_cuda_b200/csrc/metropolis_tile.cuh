@@ -482,7 +482,7 @@ template <int F>
 struct alignas(16) PRF {
     float2 f[F];
 };
-template <int NC> constexpr int kBwdA2F = (3 + 2 * NC + 1) / 2 * 2;
+template <int NC> constexpr int kBwdA2F = (3 + 2 * NC + 1) / 2 * 2;  // float2 fields
 template <int NC> using PRec = PRF<kBwdA2F<NC>>;
 
 // Stages pixel-pair records over the tile's halo: pair row i holds halo
@@ -661,6 +661,115 @@ bwd_a_tile_x2(const T* __restrict__ w, const T* __restrict__ x,
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
                     gx[cb + c * HW + q] = static_cast<T>(p == 0 ? gxa[c].x : gxa[c].y);
+            }
+        }
+    }
+}
+
+// Float2 fields per pixel-pair record holding n values: an odd number of
+// 16-byte units, so the records of 8 consecutive lanes (one 128-bit shared
+// load wavefront) fall in distinct 16-byte bank groups.
+__host__ __device__ constexpr int pair_fields(int n) {
+    return ((n + 1) / 2 * 2 / 2) % 2 == 1 ? (n + 1) / 2 * 2 : (n + 1) / 2 * 2 + 2;
+}
+
+// Aggregation for fp32 accumulators, the thread's two pixels packed as in
+// bwd_a_tile_x2 (records: r, x[NC]).  A box-masked weight contributes its
+// zero products instead of being skipped -- identical for finite inputs.
+template <int NC> constexpr int kAgg2F = pair_fields(1 + NC);
+template <typename T, int NC>
+__global__ void __launch_bounds__(NT)
+aggregate_tile_x2(const T* __restrict__ w, const T* __restrict__ x,
+                  const float* __restrict__ d, T* __restrict__ Wx,
+                  T* __restrict__ dhat, const ShiftTable st, const Geo g, int use_box,
+                  float eps) {
+    static_assert(PPT == 2, "two pixels per thread");
+    constexpr int F = kAgg2F<NC>;
+    extern __shared__ __align__(16) unsigned char smem_m[];
+    PRF<F>* rec = reinterpret_cast<PRF<F>*>(smem_m);
+    const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+    const int64_t sstride = static_cast<int64_t>(g.Cw) * HW;
+    for (int64_t grp = blockIdx.y; grp < g.groups; grp += gridDim.y) {
+        for (int64_t tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+            const Where o = where(g, tile, grp);
+            const int64_t cb = (static_cast<int64_t>(o.b) * g.C + o.c0) * HW;
+            __syncthreads();
+            const float* dg = d + grp * HW;
+            stage_pairs<F>(g, o, rec, [&](int64_t off, float* v) {
+                const float dv = dg[off];
+                v[0] = 1.f / (dv > eps ? dv : eps);
+#pragma unroll
+                for (int c = 0; c < NC; ++c) v[1 + c] = to_acc(x[cb + c * HW + off]);
+            });
+            __syncthreads();
+            const int wcol = o.w0 + threadIdx.x;
+            if (wcol >= g.W) continue;
+            const T* wb = w + (static_cast<int64_t>(o.b) * g.S * g.Cw + o.wc) * HW;
+            int hh[2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                hh[p] = h < g.H ? h : g.H - 1;
+            }
+            const int ci = (threadIdx.y + g.R) * g.XP + threadIdx.x + g.R;
+            const float2 ri = rec[ci].f[0];
+            float2 kx[NC], dh = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) kx[c] = make_float2(0.f, 0.f);
+            auto body = [&](auto border) {
+                constexpr bool BORDER = decltype(border)::value;
+#pragma unroll 2
+                for (int s = 0; s < g.S; ++s) {
+                    const int dx = st.dx[s], dy = st.dy[s];
+                    const bool inv = st.has_inv(s);
+                    const int off = dx * g.XP + dy;
+                    const T* ws = wb + s * sstride;
+                    const EdgeGeom e0 = edge_geom<BORDER>(g, hh[0], wcol, dx, dy);
+                    const EdgeGeom e1 = edge_geom<BORDER>(g, hh[1], wcol, dx, dy);
+                    float2 wq = make_float2(ldg_acc<T, float>(ws + e0.q),
+                                            ldg_acc<T, float>(ws + e1.q));
+                    float2 wm = make_float2(ldg_acc<T, float>(ws + e0.m),
+                                            ldg_acc<T, float>(ws + e1.m));
+                    if (BORDER && use_box) {
+                        if (!e0.in_p) wq.x = 0.f;
+                        if (!e1.in_p) wq.y = 0.f;
+                        if (!e0.in_m) wm.x = 0.f;
+                        if (!e1.in_m) wm.y = 0.f;
+                    }
+                    {
+                        const PRF<F> nb = rec[ci + off];
+                        const float2 wk = f2mul(wq, make_float2(fminf(ri.x, nb.f[0].x),
+                                                                fminf(ri.y, nb.f[0].y)));
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) kx[c] = f2fma(wk, nb.f[1 + c], kx[c]);
+                        dh = f2add(dh, wk);
+                    }
+                    if (inv) {
+                        const PRF<F> nb = rec[ci - off];
+                        const float2 wk = f2mul(wm, make_float2(fminf(ri.x, nb.f[0].x),
+                                                                fminf(ri.y, nb.f[0].y)));
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) kx[c] = f2fma(wk, nb.f[1 + c], kx[c]);
+                        dh = f2add(dh, wk);
+                    }
+                }
+            };
+            if (o.interior) body(std::false_type{});
+            else body(std::true_type{});
+            const PRF<F> me = rec[ci];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int h = o.h0 + threadIdx.y + TY * p;
+                if (h >= g.H) continue;
+                const float dhp = p == 0 ? dh.x : dh.y;
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int64_t oi = cb + c * HW + static_cast<int64_t>(h) * g.W + wcol;
+                    const float xv = p == 0 ? me.f[1 + c].x : me.f[1 + c].y;
+                    const float dhx = dhp * xv;
+                    Wx[oi] = static_cast<T>((xv - dhx) + (p == 0 ? kx[c].x : kx[c].y));
+                    dhat[oi] = static_cast<T>(dhp);
+                }
             }
         }
     }
