@@ -23,6 +23,7 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 
 #include "nsc_common.cuh"
 
@@ -130,6 +131,30 @@ template <typename A, int NC> constexpr int kBwdAF = rec_len<A>(3 + 2 * NC);
 // backward B: d, r, a, g_d, x[NC], gWx[NC]
 template <typename A, int NC> constexpr int kBwdBF = rec_len<A>(4 + 2 * NC);
 
+// Packed fp32 pairs: the two pixels a thread owns (rows TY apart) run as
+// the two lanes of sm_100's f32x2 arithmetic, one instruction per pair.
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{.reg .b64 a,b,c,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5}; mov.b64 c,{%6,%7};"
+        " fma.rn.f32x2 d,a,b,c; mov.b64 {%0,%1},d;}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 a,b,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5};"
+        " mul.rn.f32x2 d,a,b; mov.b64 {%0,%1},d;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 a,b,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5};"
+        " add.rn.f32x2 d,a,b; mov.b64 {%0,%1},d;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
 // ---------------------------------------------------------------- degree
 template <typename T>
 __global__ void __launch_bounds__(NT)
@@ -159,13 +184,34 @@ degree_tile(const T* __restrict__ w, typename Acc<T>::type* __restrict__ d,
                     const int dx = st.dx[s], dy = st.dy[s];
                     const bool inv = st.has_inv(s);
                     const T* ws = wb + s * sstride;
+                    if constexpr (std::is_same_v<A, float> && PPT == 2) {
+                        // fp32: both pixels' sums as one f32x2 add per term
+                        // (a masked term adds +0, which leaves every sum as is)
+                        const EdgeGeom e0 = edge_geom<BORDER>(g, hh[0], wcol, dx, dy);
+                        const EdgeGeom e1 = edge_geom<BORDER>(g, hh[1], wcol, dx, dy);
+                        float2 wq = make_float2(ldg_acc<T, float>(ws + e0.q),
+                                                ldg_acc<T, float>(ws + e1.q));
+                        float2 wm = make_float2(ldg_acc<T, float>(ws + e0.m),
+                                                ldg_acc<T, float>(ws + e1.m));
+                        if (BORDER && use_box) {
+                            if (!e0.in_p) wq.x = 0.f;
+                            if (!e1.in_p) wq.y = 0.f;
+                            if (!e0.in_m) wm.x = 0.f;
+                            if (!e1.in_m) wm.y = 0.f;
+                        }
+                        float2 a2 = f2add(make_float2(acc[0], acc[1]), wq);
+                        if (inv) a2 = f2add(a2, wm);
+                        acc[0] = a2.x;
+                        acc[1] = a2.y;
+                    } else {
 #pragma unroll
-                    for (int p = 0; p < PPT; ++p) {
-                        const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
-                        const A wq = ldg_acc<T, A>(ws + e.q);
-                        const A wm = ldg_acc<T, A>(ws + e.m);
-                        if (!use_box || e.in_p) acc[p] += wq;
-                        if (inv && (!use_box || e.in_m)) acc[p] += wm;
+                        for (int p = 0; p < PPT; ++p) {
+                            const EdgeGeom e = edge_geom<BORDER>(g, hh[p], wcol, dx, dy);
+                            const A wq = ldg_acc<T, A>(ws + e.q);
+                            const A wm = ldg_acc<T, A>(ws + e.m);
+                            if (!use_box || e.in_p) acc[p] += wq;
+                            if (inv && (!use_box || e.in_m)) acc[p] += wm;
+                        }
                     }
                 }
             };
@@ -440,30 +486,6 @@ bwd_a_tile(const T* __restrict__ w, const T* __restrict__ x,
     }
 }
 
-// Packed fp32 pairs: the two pixels a thread owns (rows TY apart) run as
-// the two lanes of sm_100's f32x2 arithmetic, one instruction per pair.
-__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
-    float2 r;
-    asm("{.reg .b64 a,b,c,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5}; mov.b64 c,{%6,%7};"
-        " fma.rn.f32x2 d,a,b,c; mov.b64 {%0,%1},d;}"
-        : "=f"(r.x), "=f"(r.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return r;
-}
-__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
-    float2 r;
-    asm("{.reg .b64 a,b,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5};"
-        " mul.rn.f32x2 d,a,b; mov.b64 {%0,%1},d;}"
-        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return r;
-}
-__device__ __forceinline__ float2 f2add(float2 a, float2 b) {
-    float2 r;
-    asm("{.reg .b64 a,b,d; mov.b64 a,{%2,%3}; mov.b64 b,{%4,%5};"
-        " add.rn.f32x2 d,a,b; mov.b64 {%0,%1},d;}"
-        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return r;
-}
 // -share(self, other) where the denominator passes gradient (max >= eps),
 // else 0: the factor of a pair's degree-gradient term.
 __device__ __forceinline__ float neg_share(float self, float other, float eps) {
