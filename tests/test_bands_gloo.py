@@ -76,12 +76,16 @@ def _worker(rank, world, port, Hg, W, R, padded, out):
         row0, Hb = bands.band_rows(Hg, world, rank)
         xb = x[:, :, row0:row0 + Hb].contiguous()
         if padded:   # spare halo rows hold NaN: the exchange must overwrite them
-            xp = torch.full((B, C, Hb + 2 * R, W), float("nan"), dtype=x.dtype)
+            if padded == "strided":   # a non-contiguous buffer: staged halo copies
+                xp = torch.full((B, Hb + 2 * R, W, C), float("nan"),
+                                dtype=x.dtype).permute(0, 3, 1, 2)
+            else:                     # contiguous: halo rows received in place
+                xp = torch.full((B, C, Hb + 2 * R, W), float("nan"), dtype=x.dtype)
             xp[:, :, R:R + Hb] = xb
             xb = xp
         U, Z = bands.accumulate_uz_banded(
             xb, w[:, :, row0:row0 + Hb].contiguous(), sh, Hg,
-            compute=_band_compute_cpu, padded=padded)
+            compute=_band_compute_cpu, padded=bool(padded))
         ok = (torch.allclose(U, U_ref[:, :, row0:row0 + Hb], rtol=1e-10, atol=1e-10)
               and torch.allclose(Z, Z_ref[:, :, row0:row0 + Hb], rtol=1e-10, atol=1e-10))
         out[rank] = 1 if ok else 0
@@ -99,7 +103,8 @@ def _free_port():
 
 @pytest.mark.parametrize("world,Hg,W,R,padded", [(2, 12, 9, 2, False), (3, 17, 7, 3, False),
                                                  (2, 8, 6, 1, False), (3, 17, 7, 3, True),
-                                                 (2, 12, 9, 2, True)])
+                                                 (2, 12, 9, 2, True),
+                                                 (3, 17, 7, 3, "strided")])
 def test_banded_accumulate_gloo(world, Hg, W, R, padded):
     ctx = mp.get_context("spawn")
     out = ctx.Array("i", [0] * world)
