@@ -20,13 +20,14 @@ identical to the unsplit op:
 
 The strips need only the rank's own rows, so they are computed first and
 both exchanges travel in ONE grouped send/recv (`batch_isend_irecv`, NCCL
-over NVLink for CUDA tensors).  On CUDA the exchange is split in two so it
-leaves the critical path: the x halo travels while the edge-strip kernel
-runs, and the strips (needed only by the final add) travel while the band
-forward runs on all SMs but a few left to NCCL's kernels.  With
-`padded=True` the caller's x buffer has R spare rows above and below the
-band and the halo is received straight into them (no band-sized copy per
-step).  The compute is injectable so the exchange logic runs on CPU `gloo`
+over NVLink for CUDA tensors); with a contiguous x buffer each (image,
+channel) plane's halo rows are sent from and received into the buffer
+itself, with no staging copies.  An overlapped form (off by default: no
+faster on 2 B200s) splits the exchange so the x halo travels while the
+edge-strip kernel runs and the strips (needed only by the final add)
+while the band forward runs.  With `padded=True` the caller's x buffer has
+R spare rows above and below the band and the halo is received straight
+into them (no band-sized copy per step).  The compute is injectable so the exchange logic runs on CPU `gloo`
 ranks in the tests.
 """
 
@@ -302,11 +303,11 @@ def accumulate_uz_banded(x_band, w_band, shifts, Hg: int, group=None,
     (U, Z, top, bot) (run after the halo arrives).  overlap=True (CUDA
     forward only): the x halo travels during the edge-strip kernel and the
     strips during the band forward, which runs on all but
-    NSC_BAND_RESERVE_SMS (default 2) SMs.  It measured no faster than one
-    grouped exchange on 2 and 4 B200s at configs[4] (4.69 vs 4.67 ms and
-    2.53 vs 2.51 ms per step: the exchange is short and the reserved SMs cost
-    the forward about what they hide), so overlap=None takes it from
-    NSC_BAND_OVERLAP=1 and defaults to off.  deadline (seconds): an exchange
+    NSC_BAND_RESERVE_SMS (default 0) SMs.  It measured no faster than one
+    grouped exchange at configs[4]: with 2 reserved SMs 4.69 vs 4.67 ms (2
+    B200s) and 2.53 vs 2.51 ms (4 B200s) per step, with none 4.66 vs 4.64 ms
+    (2 B200s, medians), so overlap=None takes it from NSC_BAND_OVERLAP=1 and
+    defaults to off.  deadline (seconds): an exchange
     that has not completed in time, or whose peer left, raises
     BandExchangeError (the process group's own timeout applies otherwise)."""
     import torch.distributed as dist
